@@ -1,0 +1,14 @@
+import os
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+PKG_ROOT = ROOT / "vllm-ascend-kvcompress-hust_b200"
+for p in (str(ROOT), str(PKG_ROOT), str(ROOT / "tests")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA B200 (sm_100a) device")
+    config.addinivalue_line("markers", "slow: takes more than a few seconds on CPU")
