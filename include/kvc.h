@@ -1,0 +1,216 @@
+/*
+ * kvc.h -- C ABI of the B200 (sm_100a) TriAttention compression hot path.
+ *
+ * Library: libkvc_b200.so.  Every entry point
+ *   - takes plain device pointers, sizes and a cudaStream_t passed as void*;
+ *   - validates its scalar arguments and pointer alignment on the host and
+ *     returns a negative KVC_E* status WITHOUT launching when they are bad;
+ *   - is asynchronous on the given stream, performs no allocation, no
+ *     host<->device copy and no synchronisation;
+ *   - reports data-dependent faults found on the device (block id or token
+ *     index out of range, budget larger than a request) by OR-ing a KVC_DEV_*
+ *     bit into the optional device word `error_flag` and skipping the access.
+ *
+ * Ragged batches use a page-padded "token space": request r owns the 128-token
+ * pages [page_off[r], page_off[r+1]) and the tokens
+ * [page_off[r]*128, page_off[r]*128 + tokens[r]) of every per-token buffer.
+ * Block tables are CSR: request r's kernel block ids are
+ * blocks[block_off[r] .. block_off[r+1]).
+ *
+ * Paths in the citations below are relative to the reference project
+ * vllm-ascend-kvcompress-hust 0.10.0 (src/vllm_ascend_kvcompress/...).
+ */
+#ifndef KVC_B200_H
+#define KVC_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KVC_ABI_VERSION 1
+
+/* host-side status codes */
+#define KVC_OK 0
+#define KVC_EINVAL (-22)      /* bad size, count or enum value */
+#define KVC_ENULL (-14)       /* required pointer is NULL */
+#define KVC_EALIGN (-71)      /* pointer or stride misaligned for the kernel */
+#define KVC_EUNSUPPORTED (-95) /* geometry not compiled (e.g. query group > 8) */
+#define KVC_ECUDA (-5)        /* the launch itself failed */
+
+/* device error bits (OR-ed into *error_flag) */
+#define KVC_DEV_BLOCK_RANGE 1   /* a block id outside [0, num_blocks) */
+#define KVC_DEV_TOKEN_RANGE 2   /* a keep index outside [0, tokens) */
+#define KVC_DEV_BUDGET 4        /* budget/windows impossible for a request */
+
+/* cache element types */
+#define KVC_BF16 0
+#define KVC_FP16 1
+
+/* aggregation / policy enums */
+#define KVC_AGG_MEAN 0
+#define KVC_AGG_MAX 1
+#define KVC_POLICY_GLOBAL 0
+#define KVC_POLICY_V3 1
+
+int kvc_abi_version(void);
+const char* kvc_status_string(int status);
+
+/* Floats per (request, scoring layer, kv head) block of `coef`:
+ * F * round_up(3*G, 4) for mean aggregation; for max aggregation
+ * F * round_up(3*G, 4) + n_off * F * 2 (the per-offset cos/sin table). */
+int64_t kvc_coef_floats(int num_freq, int group, int n_off, int aggregation);
+
+/*
+ * Phase coefficients of every (request, scoring layer):
+ *   c_f = mean_o cos(fp32(offset_o + round_start[r]) * omega[l][f]),
+ *   s_f = mean_o sin(...), then per (kv head h, q head g, frequency f)
+ *   a = scale*(qr*c - qi*s), b = scale*(qi*c + qr*s), e = extra*scale.
+ * Replaces prepare_mean_phase_coefficients (methods/triattention/kernels.py:85-122)
+ * and the phase formation of score_post_rope_keys (methods/triattention/scoring.py:77-83),
+ * computed directly per request (no angle-addition shortcut).
+ * omega [L][F]; q_real, q_imag, scale, extra [L][kvh][G][F] (fp32);
+ * offsets [n_off]; round_start [R] (int64, device). coef_out: R*L*kvh*kvc_coef_floats.
+ */
+int kvc_prepare_score_coefficients(const float* omega, const float* offsets, int n_off,
+                                   const int64_t* round_start, int num_requests,
+                                   int num_layers, int kv_heads, int group, int num_freq,
+                                   const float* q_real, const float* q_imag,
+                                   const float* scale, const float* extra,
+                                   int aggregation, float* coef_out, void* stream);
+
+/*
+ * Raw trigonometric scores of every cached key of every request in every
+ * scoring layer, plus per-page partial moments for the per-head statistics.
+ * Replaces score_paged_keys_mean_precomputed (methods/triattention/kernels.py:247-317)
+ * and the CPU chunk loop of TriAttentionMethod._select_keep_indices
+ * (methods/triattention/method.py:405-422), batched over requests and layers.
+ *   k_layers     host array [num_layers] of K cache base pointers, each
+ *                [num_blocks][128][kv_heads][head_dim] with contiguous inner
+ *                dims and `block_stride` elements between blocks.
+ *   coef         output of kvc_prepare_score_coefficients (same aggregation).
+ *   q_pass_t     [L][kvh][head_dim-rotary_dim][G] fp32 (transposed q_pass_mean),
+ *                NULL for full RoPE.
+ *   raw_out      [L][kvh*G][total_pages*128] fp32.
+ *   partial_out  [L][total_pages][kvh*G][2] fp32: (page sum, page sum of
+ *                squared deviations from the page mean).
+ */
+int kvc_score_paged_keys(const void* const* k_layers, int num_layers, int dtype,
+                         int64_t block_stride, int64_t num_blocks, int kv_heads, int group,
+                         int head_dim, int rotary_dim, const int64_t* src_blocks,
+                         const int64_t* src_block_off, const int32_t* tokens,
+                         const int32_t* page_off, int num_requests, int total_pages,
+                         const float* coef, int n_off, int aggregation, const float* q_pass_t,
+                         float* raw_out, float* partial_out, int32_t* error_flag, void* stream);
+
+/*
+ * Per (scoring layer, request, query head) population mean/variance of the
+ * raw scores, combined from the page moments in fp64; denom = sqrt(max(var, 1e-6)).
+ * Replaces torch.var_mean(raw, dim=-1, correction=0) (methods/triattention/method.py:379-381,423)
+ * and the denominator of normalize_head_scores (methods/triattention/scoring.py:123-128).
+ * mean_out, var_out, denom_out: [L][R][kvh*G].
+ */
+int kvc_head_stats(const float* partial, int num_layers, int num_requests, int total_pages,
+                   int heads, const int32_t* tokens, const int32_t* page_off, float* mean_out,
+                   float* var_out, float* denom_out, void* stream);
+
+/*
+ * Normalise (z = (raw - mean) / denom), max over the local query heads, then
+ * either write one row per scoring layer (rows_out [L][total_pages*128], the
+ * tensor-parallel all-reduce input) or, when rows_out is NULL, reduce the
+ * layers (sum then / L, or max) and finalise (NaN -> -inf, +inf -> 1e30) into
+ * agg_out [total_pages*128].
+ * Replaces aggregate_normalized_scores (methods/triattention/kernels.py:407-437),
+ * TriAttentionMethod._aggregate_torch (methods/triattention/method.py:477-503)
+ * and the finalisation at methods/triattention/method.py:463-467.
+ */
+int kvc_normalize_aggregate(const float* raw, int num_layers, int heads, int total_pages,
+                            const float* mean, const float* denom, const int32_t* tokens,
+                            const int32_t* page_off, int num_requests, int layer_aggregation,
+                            float* rows_out, float* agg_out, void* stream);
+
+/*
+ * Layer reduction of the (all-reduced) per-layer rows and finalisation.
+ * Replaces methods/triattention/method.py:458-467 (torch.sum/amax over the
+ * TP-synchronised parallel_scores, mean, nan_to_num).
+ */
+int kvc_aggregate_rows(const float* rows, int num_layers, int total_pages,
+                       const int32_t* tokens, const int32_t* page_off, int num_requests,
+                       int layer_aggregation, float* agg_out, void* stream);
+
+/*
+ * Ragged segmented selection: for every request keep exactly `budget`
+ * positions, sorted ascending: the protected prefix and recent windows plus,
+ * per V3 segment (or the whole middle for the global policy), the top-quota
+ * scores; equal scores are taken lowest position first.
+ * Replaces select_keep_indices (methods/triattention/selection.py:108-196,
+ * including the batched V3 plan of :24-105).  keep_out [R][budget] int64.
+ */
+int kvc_select_keep(const float* agg, const int32_t* tokens, const int32_t* page_off,
+                    int num_requests, int budget, int prefix, int recent, int segments,
+                    int policy, int64_t* keep_out, int32_t* error_flag, void* stream);
+
+/*
+ * Compaction of every layer: for each request r and j < budget, copy the K and
+ * V rows of token keep[r][j] (through the source block table) into dense
+ * position j of the destination block table.  Source and destination blocks
+ * must be disjoint (the provider guarantees private destinations).
+ * Optionally stages the commit: staged_rows[r][:] = destination block ids,
+ * staged_offsets[r] = semantic[r] - budget (the request's position offset).
+ * Replaces the per-layer materialize_token_slots loop
+ * (methods/triattention/method.py:272-288, methods/triattention/cache.py:9-15,100-111).
+ *   k_layers, v_layers  host arrays [num_layers] of cache base pointers.
+ *   row_bytes           kv_heads*head_dim*element size (one token, all local heads).
+ */
+int kvc_compact(const void* const* k_layers, const void* const* v_layers, int num_layers,
+                int64_t block_stride_bytes, int64_t num_blocks, int64_t row_bytes,
+                const int64_t* src_blocks, const int64_t* src_block_off,
+                const int64_t* dst_blocks, const int64_t* dst_block_off, const int64_t* keep,
+                const int32_t* tokens, int num_requests, int budget,
+                int64_t* staged_rows, int staged_row_stride, int64_t* staged_offsets,
+                const int64_t* semantic, int32_t* error_flag, void* stream);
+
+/*
+ * Slot gather / scatter through a workspace: out[i] = cache[slot[i]] and
+ * cache[slot[i]] = in[i] (slot = block*block_size + within).  Gathering all
+ * rows before scattering makes overlapping source/destination slots safe.
+ * Replaces _gather_slots/_write_slots/materialize_token_slots
+ * (methods/triattention/cache.py:18-45,100-111).
+ */
+int kvc_gather_slots(const void* cache, int64_t block_stride_bytes, int block_size,
+                     int64_t num_blocks, int64_t row_bytes, const int64_t* slots, int64_t n,
+                     void* out, int32_t* error_flag, void* stream);
+int kvc_scatter_slots(void* cache, int64_t block_stride_bytes, int block_size,
+                      int64_t num_blocks, int64_t row_bytes, const int64_t* slots, int64_t n,
+                      const void* in, int32_t* error_flag, void* stream);
+
+/*
+ * Calibration reduction of pre-RoPE queries q [n_tokens][row_stride] (heads *
+ * head_dim used per row): per (head, frequency) sums of re = q[f],
+ * im = q[F + f], |.| = sqrt(re^2 + im^2), and per (head, pass dim) sums of
+ * q[rotary_dim + p], accumulated (+=) into fp64 outputs.
+ * Replaces _LayerAccumulator.add (calibration.py:95-131).
+ * workspace: kvc_calibration_workspace_doubles(...) doubles.
+ */
+int64_t kvc_calibration_workspace_doubles(int64_t n_tokens, int heads, int head_dim,
+                                          int rotary_dim);
+int kvc_calibration_accumulate(const void* q, int dtype, int64_t n_tokens, int64_t row_stride,
+                               int heads, int head_dim, int rotary_dim, double* re_sum,
+                               double* im_sum, double* abs_sum, double* pass_sum,
+                               double* workspace, int64_t workspace_doubles, void* stream);
+
+/*
+ * Physical decode positions: out[i] = positions[i] - offsets[request_indices[i]].
+ * Replaces shift_positions (methods/triattention/kernels.py:35-47).
+ * index_bytes: 4 (int32 request indices) or 8 (int64).
+ */
+int kvc_shift_positions(const int64_t* positions, const void* request_indices, int index_bytes,
+                        const int64_t* offsets, int64_t num_offsets, int64_t n, int64_t* out,
+                        int32_t* error_flag, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVC_B200_H */

@@ -272,3 +272,61 @@ def golden_selection_scores(cases: list) -> list[torch.Tensor]:
     ``torch.manual_seed(28)`` (the reference test's recipe), one per case."""
     torch.manual_seed(28)
     return [torch.randperm(c[0], dtype=torch.long).float() for c in cases]
+
+
+# ---------------------------------------------------------------------------
+# binding helpers for this repository's B200 package (imported lazily so the
+# golden script, which imports the reference package of the same name, never
+# touches them)
+# ---------------------------------------------------------------------------
+
+
+def layer_name(i: int) -> str:
+    return f"model.layers.{i}.self_attn.attn"
+
+
+def b200_method(w: Workload, caches, stats_path: str, *, tp_size: int = 1, tp_group=None, tp_rank=None,
+                device="cuda", options: Options | None = None, geometry: Geometry | None = None):
+    """Bind this package's TriAttentionMethod to ``caches`` [(k, v) per layer]."""
+    from types import SimpleNamespace
+
+    from vllm_ascend_kvcompress.methods.base import LayerCache, ModelShape
+    from vllm_ascend_kvcompress.methods.triattention.method import TriAttentionMethod
+
+    geo = geometry or w.geometry
+    opts = options or w.options
+    shape = ModelShape(model_type=geo.model_type, num_layers=geo.num_layers, num_attention_heads=geo.num_q_heads,
+                       num_kv_heads=geo.num_kv_heads, head_dim=geo.head_dim, rope_theta=geo.rope_theta,
+                       has_rope_scaling=False,
+                       rotary_dim=None if geo.rotary_dim == geo.head_dim else geo.rotary_dim)
+    vcfg = SimpleNamespace(parallel_config=SimpleNamespace(tensor_parallel_size=tp_size),
+                           model_config=SimpleNamespace(max_model_len=opts.max_model_len),
+                           speculative_config=None)
+    m = TriAttentionMethod(opts.method_config(stats_path), vcfg, shape)
+    runner = SimpleNamespace(device=torch.device(device), kvc_tp_group=tp_group, kvc_tp_rank=tp_rank)
+    layers = tuple(LayerCache(name=layer_name(i), layer_index=i, k_cache=k, v_cache=v)
+                   for i, (k, v) in enumerate(caches))
+    m.bind_model_runner(runner, layers)
+    return m
+
+
+def b200_requests(w: Workload, device="cuda", indices: list[int] | None = None):
+    """CompressionRequest objects of the workload's compressed sequences."""
+    from vllm_ascend_kvcompress.methods.base import CompressionRequest
+
+    out = []
+    for i in (indices if indices is not None else w.compressed()):
+        out.append(CompressionRequest(
+            request_id=f"r{i}", semantic_num_tokens=w.lengths[i], physical_num_tokens=w.lengths[i],
+            source_block_ids=(tuple(w.src_tables[i]),), destination_block_ids=(tuple(w.dst_tables[i]),),
+            source_block_ids_device=torch.tensor(w.src_tables[i], dtype=torch.long, device=device),
+            destination_block_ids_device=torch.tensor(w.dst_tables[i], dtype=torch.long, device=device)))
+    return out
+
+
+def write_stats_file(w: Workload, directory) -> str:
+    from pathlib import Path
+
+    path = Path(directory) / f"{w.name}-stats.pt"
+    torch.save(calibration_payload(w.geometry, w.seed), path)
+    return str(path)

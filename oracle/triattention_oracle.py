@@ -452,3 +452,20 @@ class CalibrationSums:
 def shift_positions(positions, request_indices, request_offsets):
     """Physical decode positions (kernels.py:35-47): pos - offsets[req]."""
     return positions - request_offsets.index_select(0, request_indices.to(torch.long))
+
+
+def stats_from_payload(payload: dict, num_kv_heads: int, group: int, rotary_dim: int,
+                       layers: Sequence[int]) -> list[LayerStats]:
+    """LayerStats per layer from a schema-3 payload whose rows are per query head.
+
+    Query heads are grouped kv-major ``[kvh, G, F]`` as stats.py:345-360 does.
+    """
+    out = []
+    g = lambda t: t.float().reshape(num_kv_heads, group, -1).contiguous()
+    for li in layers:
+        e = payload["layer_stats"][str(li)]
+        out.append(LayerStats(
+            q_mean_real=g(e["q_mean_real"]), q_mean_imag=g(e["q_mean_imag"]), q_abs_mean=g(e["q_abs_mean"]),
+            freq_scale_sq=g(e["freq_scale_sq"]), omega=e["inv_freq"].float().contiguous(), rotary_dim=rotary_dim,
+            q_pass_mean=g(e["q_pass_mean"]) if "q_pass_mean" in e else None))
+    return out

@@ -1,0 +1,101 @@
+"""The C ABI library loads without a GPU, exports every declared entry point,
+and rejects bad scalar arguments on the host before launching anything."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from vllm_ascend_kvcompress import _native as N
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "kvc.h"
+
+
+def declared_symbols() -> set[str]:
+    text = HEADER.read_text()
+    return set(re.findall(r"^\s*(?:int|int64_t|const char\*)\s+(kvc_\w+)\(", text, re.M))
+
+
+def test_library_loads_and_reports_abi_version():
+    lib = N.lib()
+    assert lib.kvc_abi_version() == N.ABI_VERSION
+
+
+def test_every_declared_symbol_is_exported_and_bound():
+    lib = N.lib()
+    syms = declared_symbols()
+    assert len(syms) >= 15
+    for s in syms:
+        assert hasattr(lib, s), s
+    assert syms == set(N.exported_symbols())
+
+
+def test_status_strings():
+    lib = N.lib()
+    assert lib.kvc_status_string(0) == b"ok"
+    assert b"NULL" in lib.kvc_status_string(-14)
+
+
+def test_coef_floats_layout():
+    lib = N.lib()
+    assert lib.kvc_coef_floats(64, 5, 17, 0) == 64 * 16
+    assert lib.kvc_coef_floats(32, 8, 17, 0) == 32 * 24
+    assert lib.kvc_coef_floats(64, 5, 17, 1) == 64 * 16 + 17 * 64 * 10
+
+
+def test_host_validation_rejects_without_launch():
+    lib = N.lib()
+    fake = ctypes.c_void_p(0x1000)
+    # NULL pointers
+    assert lib.kvc_select_keep(None, None, None, 1, 10, 0, 0, 8, 1, None, None, None) == -14
+    # budget 0 / windows larger than the budget / unknown policy
+    assert lib.kvc_select_keep(fake, fake, fake, 1, 0, 0, 0, 8, 1, fake, None, None) == -22
+    assert lib.kvc_select_keep(fake, fake, fake, 1, 10, 6, 6, 8, 1, fake, None, None) == -22
+    assert lib.kvc_select_keep(fake, fake, fake, 1, 10, 0, 0, 8, 7, fake, None, None) == -22
+    # score: query group above the compiled maximum
+    ptrs = N.pointer_array([0x100000])
+    rc = lib.kvc_score_paged_keys(ptrs, 1, 0, 128 * 8 * 128, 10, 8, 9, 128, 128, fake, fake, fake, fake, 1, 1,
+                                  fake, 17, 0, None, fake, fake, None, None)
+    assert rc in (-22, -95)
+    # score: frequency count not a multiple of 8 on the streaming (mean) kernel
+    rc = lib.kvc_score_paged_keys(ptrs, 1, 0, 128 * 8 * 4, 10, 8, 4, 4, 4, fake, fake, fake, fake, 1, 1,
+                                  fake, 17, 0, None, fake, fake, None, None)
+    assert rc == -95
+    # compaction: misaligned layer pointer (odd address)
+    k = N.pointer_array([0x100001])
+    v = N.pointer_array([0x200000])
+    rc = lib.kvc_compact(k, v, 1, 128 * 2048, 10, 2048, fake, fake, fake, fake, fake, fake, 1, 128,
+                         None, 0, None, None, None, None)
+    assert rc == -71
+    # compaction: block stride smaller than a page
+    rc = lib.kvc_compact(N.pointer_array([0x100000]), v, 1, 1024, 10, 2048, fake, fake, fake, fake, fake, fake,
+                         1, 128, None, 0, None, None, None, None)
+    assert rc == -22
+    # calibration: rotary dim above head dim; workspace too small
+    assert lib.kvc_calibration_accumulate(fake, 0, 10, 64, 1, 64, 128, fake, fake, fake, None, fake, 1000,
+                                          None) == -22
+    assert lib.kvc_calibration_accumulate(fake, 0, 10000, 64, 1, 64, 64, fake, fake, fake, None, fake, 1,
+                                          None) == -22
+    # shift positions: bad index width
+    assert lib.kvc_shift_positions(fake, fake, 2, fake, 1, 1, fake, None, None) == -22
+
+
+def test_check_raises_with_status_text():
+    with pytest.raises(RuntimeError, match="EINVAL"):
+        N.check(-22, "kvc_test")
+
+
+def test_kernels_refuse_cpu_tensors():
+    import torch
+
+    from vllm_ascend_kvcompress.methods.triattention import kernels as K
+    from vllm_ascend_kvcompress.methods.triattention.selection import select_keep_indices
+
+    with pytest.raises(RuntimeError, match="CUDA"):
+        select_keep_indices(torch.arange(16.0), budget=12, protected_prefix=2, protected_recent=2, segments=4,
+                            policy="v3")
+    with pytest.raises(RuntimeError, match="CUDA"):
+        K.require_cuda(torch.zeros(1))

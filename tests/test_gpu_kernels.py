@@ -1,0 +1,271 @@
+"""GPU known-answer and golden tests of the individual kernels through the C ABI.
+
+Known answers restate the literal cases of the reference's tests
+(tests/test_scoring.py, test_selection.py, test_cache.py, run_npu_kernel_smoke.py);
+golden selections come from running the reference's select_keep_indices.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import kvc_workloads as W
+from cases import golden
+from oracle import triattention_oracle as O
+from vllm_ascend_kvcompress import _native as N
+from vllm_ascend_kvcompress.calibration import LayerAccumulator
+from vllm_ascend_kvcompress.methods.triattention import kernels as K
+from vllm_ascend_kvcompress.methods.triattention.cache import (
+    gather_paged_tokens,
+    materialize_selected_tokens,
+    materialize_token_slots,
+    token_slots,
+)
+from vllm_ascend_kvcompress.methods.triattention.selection import select_keep_indices
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+
+
+# ---- selection -----------------------------------------------------------
+
+
+def test_selection_matches_reference_golden():
+    arrays, spec = golden()
+    cases = spec["selection"]
+    scores = W.golden_selection_scores(cases)
+    for n, (t, b, p, r, s, pol) in enumerate(cases):
+        keep = select_keep_indices(scores[n].to(dev), budget=b, protected_prefix=p, protected_recent=r,
+                                   segments=s, policy=pol)
+        assert np.array_equal(keep.cpu().numpy(), arrays[f"selection/{n}/keep"]), (t, b, p, r, s, pol)
+
+
+def test_selection_known_answers():
+    keep = select_keep_indices(torch.arange(16, dtype=torch.float32, device=dev), budget=12, protected_prefix=2,
+                               protected_recent=2, segments=4, policy="v3")
+    assert set(range(16)) - set(keep.tolist()) == {2, 5, 8, 11}
+    keep = select_keep_indices(torch.tensor([10.0, 9.0, 8.0, 7.0, -5.0, -6.0], device=dev), budget=4,
+                               protected_prefix=0, protected_recent=2, segments=8, policy="global")
+    assert keep.tolist() == [0, 1, 4, 5]
+    keep = select_keep_indices(torch.zeros(19, device=dev), budget=13, protected_prefix=2, protected_recent=2,
+                               segments=8, policy="v3")
+    assert keep.numel() == 13 and {0, 1, 17, 18} <= set(keep.tolist())
+
+
+def test_selection_ties_take_lowest_positions():
+    scores = torch.zeros(1000, device=dev)
+    keep = select_keep_indices(scores, budget=300, protected_prefix=0, protected_recent=0, segments=1,
+                               policy="v3").tolist()
+    assert keep == list(range(300))
+    s = torch.tensor([1.0, 5.0, 5.0, 5.0, 0.0, 5.0, 2.0], device=dev)
+    keep = select_keep_indices(s, budget=3, protected_prefix=0, protected_recent=0, segments=1, policy="global")
+    assert keep.tolist() == [1, 2, 3]
+
+
+def test_selection_special_values_and_validation():
+    s = torch.tensor([float("-inf"), 1e30, -1.0, 3.0, float("-inf"), 0.5, -0.0, 0.0], device=dev)
+    keep = select_keep_indices(s, budget=4, protected_prefix=0, protected_recent=0, segments=1, policy="v3")
+    assert keep.tolist() == [1, 3, 5, 7] or keep.tolist() == [1, 3, 5, 6]
+    with pytest.raises(ValueError, match="budget"):
+        select_keep_indices(s, budget=9, protected_prefix=0, protected_recent=0, segments=1, policy="v3")
+    with pytest.raises(ValueError, match="protected"):
+        select_keep_indices(s, budget=4, protected_prefix=3, protected_recent=2, segments=1, policy="v3")
+
+
+@pytest.mark.parametrize("t,b,p,r,s", [(65536, 4608, 128, 512, 8), (50000, 49999, 0, 0, 7), (4736, 4608, 128, 512, 8),
+                                       (9000, 1000, 0, 0, 1), (3000, 2000, 1000, 1000, 8)])
+def test_selection_random_vs_oracle(t, b, p, r, s):
+    g = torch.Generator().manual_seed(t + b)
+    scores = torch.randn(t, generator=g)
+    ref = O.select_keep_indices(scores, budget=b, protected_prefix=p, protected_recent=r, segments=s, policy="v3")
+    got = select_keep_indices(scores.to(dev), budget=b, protected_prefix=p, protected_recent=r, segments=s,
+                              policy="v3")
+    assert torch.equal(got.cpu(), ref)
+
+
+# ---- paged cache API -----------------------------------------------------
+
+
+def test_gather_maps_logical_tokens_through_block_table():
+    cache = torch.arange(12, dtype=torch.float32, device=dev).view(3, 4, 1, 1)
+    got = gather_paged_tokens(cache, torch.tensor([2, 0], device=dev), torch.tensor([0, 3, 4, 7], device=dev), 4)
+    assert got.flatten().tolist() == [8.0, 11.0, 0.0, 3.0]
+
+
+def test_materialize_overlapping_destination_gathers_first():
+    k = torch.arange(16, dtype=torch.float32, device=dev).view(4, 4, 1, 1)
+    v = k.clone() + 100
+    src, keep = torch.tensor([2, 0, 3], device=dev), torch.tensor([1, 4, 6, 9], device=dev)
+    ek = gather_paged_tokens(k, src, keep, 4).clone()
+    ev = gather_paged_tokens(v, src, keep, 4).clone()
+    materialize_selected_tokens(k, v, src, torch.tensor([2], device=dev), keep, 4)
+    torch.testing.assert_close(k[2], ek)
+    torch.testing.assert_close(v[2], ev)
+
+
+def test_padded_interleaved_pages_keep_unused_bytes():
+    bs, nb, heads, dim = 4, 4, 1, 2
+    page = bs * heads * dim
+    stride = 2 * page + 4
+    raw = torch.full((nb * stride,), -1, dtype=torch.float16, device=dev)
+    shape, strides = (nb, bs, heads, dim), (stride, heads * dim, dim, 1)
+    k = torch.as_strided(raw, shape, strides)
+    v = torch.as_strided(raw, shape, strides, storage_offset=page)
+    k.copy_(torch.arange(nb * page, device=dev).view(shape))
+    v.copy_(torch.arange(nb * page, device=dev).view(shape) + 100)
+    src, keep = torch.tensor([2, 0, 3], device=dev), torch.tensor([1, 4, 6, 9], device=dev)
+    ek = gather_paged_tokens(k, src, keep, bs).clone()
+    ev = gather_paged_tokens(v, src, keep, bs).clone()
+    materialize_selected_tokens(k, v, src, torch.tensor([2], device=dev), keep, bs)
+    torch.testing.assert_close(k[2], ek)
+    torch.testing.assert_close(v[2], ev)
+    s_slots = token_slots(torch.tensor([2], device=dev), torch.arange(4, device=dev), bs)
+    d_slots = token_slots(torch.tensor([1], device=dev), torch.arange(4, device=dev), bs)
+    materialize_token_slots(k, v, s_slots, d_slots, torch.empty_like(ek), torch.empty_like(ev))
+    torch.testing.assert_close(k[1], ek)
+    torch.testing.assert_close(v[1], ev)
+    torch.testing.assert_close(raw.view(nb, stride)[:, -4:], torch.full((nb, 4), -1, dtype=torch.float16, device=dev))
+
+
+def test_gather_slot_out_of_range_is_flagged():
+    cache = torch.zeros(3, 4, 1, 2, device=dev)
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    K.gather_slots(cache, torch.tensor([0, 12, 5], device=dev), error_flag=flag)
+    assert int(flag) & N.DEV_BLOCK_RANGE
+
+
+def test_shift_positions_known_answer():
+    out = torch.empty(3, dtype=torch.int64, device=dev)
+    K.shift_positions(torch.tensor([300, 20, 301], device=dev), torch.tensor([0, 1, 0], device=dev),
+                      torch.tensor([172, 0], device=dev), out)
+    assert out.tolist() == [128, 20, 129]
+    K.shift_positions(torch.tensor([300, 20, 301], device=dev), torch.tensor([0, 1, 0], device=dev, dtype=torch.int32),
+                      torch.tensor([172, 0], device=dev), out)
+    assert out.tolist() == [128, 20, 129]
+
+
+# ---- scoring known answers (embedded in an 8-frequency paged cache) ------
+
+
+def _score_small(keys: torch.Tensor, qr, qi, qabs, fsq, omega, rot_small: int, q_pass=None, round_start: int = 1,
+                 offsets=(1.0,)):
+    """Score tiny half-RoPE keys ``[T, 1, D]`` by zero-padding F to 8 and P to 8 (zeros add nothing)."""
+    T, _, d = keys.shape
+    f_small = rot_small // 2
+    p_small = d - rot_small
+    F, P = 8, (8 if p_small else 0)
+    D = 2 * F + P
+    G = qr.shape[1]
+    padded = torch.zeros(T, 1, D)
+    padded[:, 0, :f_small] = keys[:, 0, :f_small]
+    padded[:, 0, F:F + f_small] = keys[:, 0, f_small:rot_small]
+    if p_small:
+        padded[:, 0, 2 * F:2 * F + p_small] = keys[:, 0, rot_small:]
+    pages = -(-T // 128)
+    cache = torch.zeros(pages, 128, 1, D, dtype=torch.bfloat16)
+    cache.view(-1, 1, D)[:T] = padded.to(torch.bfloat16)
+    cache = cache.to(dev)
+
+    def pad_f(t):
+        out = torch.zeros(1, G, F)
+        out[..., :f_small] = t
+        return out
+
+    omega_p = torch.zeros(F)
+    omega_p[:f_small] = omega
+    scale = torch.sqrt(pad_f(fsq))
+    qmag = torch.sqrt(pad_f(qr).square() + pad_f(qi).square() + 1e-8)
+    extra = pad_f(qabs) - qmag
+    extra[..., f_small:] = 0.0
+    meta = torch.tensor([T, 0, pages], dtype=torch.int32, device=dev)
+    i64 = torch.tensor([0, pages, 0, 1, round_start, round_start], dtype=torch.int64, device=dev)
+    plan = K.BatchPlan(1, pages, meta[:1], meta[1:], torch.arange(pages, device=dev), i64[:2], i64[:0], i64[2:4],
+                       i64[4:5], i64[5:6], (T,), 0)
+    offs = torch.tensor(offsets, device=dev)
+    coef = torch.empty(K.coef_floats(F, G, offs.numel(), N.AGG_MEAN), device=dev)
+    K.prepare_score_coefficients(omega_p[None].to(dev).contiguous(), offs, plan, pad_f(qr)[None].to(dev).contiguous(),
+                                 pad_f(qi)[None].to(dev).contiguous(), scale[None].to(dev).contiguous(),
+                                 extra[None].to(dev).contiguous(), N.AGG_MEAN, coef)
+    qp = None
+    if p_small:
+        qpp = torch.zeros(1, G, P)
+        qpp[..., :p_small] = q_pass
+        qp = qpp.transpose(-1, -2).contiguous()[None].to(dev).contiguous()
+    raw = torch.empty(G * pages * 128, device=dev)
+    part = torch.empty(pages * G * 2, device=dev)
+    K.score_paged_keys(N.pointer_array([cache.data_ptr()]), torch.bfloat16, cache.stride(0), pages, 1, G, D,
+                       2 * F, plan, coef, offs.numel(), N.AGG_MEAN, qp, raw, part, None)
+    return raw.view(G, -1)[:, :T].cpu()
+
+
+def test_score_query_side_scale_gives_four():
+    got = _score_small(torch.tensor([[[2.0, 0.0]]]), torch.ones(1, 1, 1), torch.zeros(1, 1, 1), torch.ones(1, 1, 1),
+                       torch.full((1, 1, 1), 4.0), torch.zeros(1), rot_small=2)
+    torch.testing.assert_close(got, torch.tensor([[4.0]]))
+
+
+def test_score_partial_rope_content_term():
+    got = _score_small(torch.tensor([[[0.0, 0.0, 3.0, 4.0]], [[0.0, 0.0, -2.0, 1.0]]]), torch.zeros(1, 1, 1),
+                       torch.zeros(1, 1, 1), torch.zeros(1, 1, 1), torch.ones(1, 1, 1), torch.zeros(1), rot_small=2,
+                       q_pass=torch.tensor([[[2.0, -1.0]]]))
+    torch.testing.assert_close(got, torch.tensor([[2.0, -5.0]]))
+
+
+def test_score_mean_over_offsets_matches_oracle():
+    keys = torch.tensor([[[1.0, 2.0, 3.0, 4.0]], [[0.5, 1.5, 2.5, 3.5]], [[2.0, 1.0, 4.0, 3.0]]])
+    st = O.LayerStats(torch.tensor([[[1.0, 0.5], [0.25, 0.75]]]), torch.tensor([[[0.0, 0.5], [0.5, 0.25]]]),
+                      torch.ones(1, 2, 2), torch.ones(1, 2, 2), torch.tensor([1.0, 0.1]))
+    ref = O.score_keys(keys, st, round_start=3, offsets=torch.tensor([1.0, 2.0, 4.0]))[0]
+    got = _score_small(keys, st.q_mean_real, st.q_mean_imag, st.q_abs_mean, st.freq_scale_sq, st.omega, rot_small=4,
+                       round_start=3, offsets=(1.0, 2.0, 4.0))
+    torch.testing.assert_close(got, ref, rtol=1e-5, atol=1e-5)
+
+
+# ---- calibration ------------------------------------------------------------
+
+
+@pytest.mark.parametrize("case", ["calib_full", "calib_partial"])
+def test_calibration_matches_reference_golden(case):
+    arrays, spec = golden()
+    inputs = {n: (h, d, r, q) for n, h, d, r, q in W.golden_calibration_inputs()}
+    heads, hd, rot, calls = inputs[case]
+    acc = LayerAccumulator()
+    for q in calls:
+        acc.add(q.to(dev), heads, hd, rot)
+    assert acc.count == spec[case]["count"]
+    for k in ("real_sum", "imag_sum", "abs_sum", "pass_sum"):
+        key = f"{case}/{k}"
+        if key in arrays:
+            torch.testing.assert_close(getattr(acc, k).float().cpu(), torch.from_numpy(arrays[key]), rtol=1e-5, atol=1e-4)
+
+
+def test_calibration_large_vs_fp64_and_packed_gate():
+    heads, hd, rot = 40, 128, 128
+    q = W.calibration_queries(0, 2, 8192, heads, hd, device=dev)
+    acc = LayerAccumulator()
+    acc.add(q[:10000], heads, hd, rot)
+    gate = torch.cat([q[10000:], torch.randn_like(q[10000:])], dim=1)  # Qwen3.5 packs the gate after Q
+    acc.add(gate, heads, hd, rot)
+    v = q.cpu().double().reshape(-1, heads, hd)
+    re, im = v[..., : rot // 2], v[..., rot // 2: rot]
+    want_all = {"q_mean_real": re.mean(0), "q_mean_imag": im.mean(0),
+                "q_abs_mean": torch.sqrt(re.square() + im.square()).mean(0)}
+    mean_abs = v.abs().mean().item()
+    got = acc.means()
+    for k, want in want_all.items():
+        err = (got[k].double() - want).abs().max().item()
+        assert err <= 1e-4 * max(want.abs().max().item(), mean_abs), (k, err)
+
+
+def test_calibration_partial_rope_unaligned_widths():
+    heads, hd, rot = 3, 20, 6  # F = 3, P = 14: falls back to narrow vectors
+    q = torch.randn(777, heads * hd, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16)
+    acc = LayerAccumulator()
+    acc.add(q.to(dev), heads, hd, rot)
+    ref = O.CalibrationSums()
+    ref.add(q.double(), heads, hd, rot)
+    torch.testing.assert_close(acc.real_sum.float().cpu(), ref.real_sum, rtol=1e-5, atol=1e-4)
+    torch.testing.assert_close(acc.abs_sum.float().cpu(), ref.abs_sum, rtol=1e-5, atol=1e-4)
+    torch.testing.assert_close(acc.pass_sum.float().cpu(), ref.pass_sum, rtol=1e-5, atol=1e-4)

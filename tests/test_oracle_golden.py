@@ -14,7 +14,7 @@ import pytest
 import torch
 
 import kvc_workloads as W
-from cases import (
+from cases import (  # noqa: I001
     cpu_caches,
     golden,
     golden_small_cases,

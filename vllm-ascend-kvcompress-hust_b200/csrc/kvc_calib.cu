@@ -1,0 +1,183 @@
+// Calibration reduction of pre-RoPE queries on sm_100a.
+//
+// Columns: a "rope unit" is (head, V consecutive frequencies) -- the thread
+// reads V real parts q[f..f+V) and the matching V imaginary parts
+// q[F+f..F+f+V) (16-byte vectors when V = 8) -- and a "pass unit" is (head, V
+// consecutive unrotated dims).  Each thread sums its column over a fixed chunk
+// of tokens in fp32 (|q| = sqrt(re^2 + im^2) per element) and writes the chunk
+// partial; a second kernel adds the chunk partials in a fixed order in fp64
+// into the caller's running fp64 sums (deterministic, atomics-free).
+#include "kvc_common.cuh"
+
+namespace kvc {
+
+constexpr int kCalibChunk = 512;   // tokens per partial
+constexpr int kCalibThreads = 256;
+
+struct CalibArgs {
+  const uint16_t* q;
+  int64_t n_tok, row_stride;
+  int H, D, F, P, V;
+  int rope_cols, cols;
+  double* ws;  // [nchunk][cols][3V]
+};
+
+template <int V, class E>
+__device__ __forceinline__ void load_vals(const uint16_t* p, float (&x)[V]) {
+  if constexpr (V == 8) {
+    const uint4 v = ldg_stream16(p);
+    x[0] = elem8<0>(v, E{}); x[1] = elem8<1>(v, E{}); x[2] = elem8<2>(v, E{}); x[3] = elem8<3>(v, E{});
+    x[4] = elem8<4>(v, E{}); x[5] = elem8<5>(v, E{}); x[6] = elem8<6>(v, E{}); x[7] = elem8<7>(v, E{});
+  } else if constexpr (V == 2) {
+    const float2 t = unpack2(__ldg(reinterpret_cast<const uint32_t*>(p)), E{});
+    x[0] = t.x; x[1] = t.y;
+  } else {
+    x[0] = unpack1(__ldg(p), E{});
+  }
+}
+
+template <int V, class E>
+__global__ void __launch_bounds__(kCalibThreads) calib_partial_kernel(const __grid_constant__ CalibArgs a) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= a.cols) return;
+  const int64_t t0 = (int64_t)blockIdx.y * kCalibChunk;
+  const int64_t t1 = min64(a.n_tok, t0 + kCalibChunk);
+  double* out = a.ws + ((int64_t)blockIdx.y * a.cols + col) * 3 * V;
+  if (col < a.rope_cols) {
+    const int per = a.F / V;
+    const int h = col / per, f = (col % per) * V;
+    const uint16_t* base = a.q + (int64_t)h * a.D + f;
+    float re[V], im[V], ab[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) re[j] = im[j] = ab[j] = 0.f;
+    for (int64_t t = t0; t < t1; ++t) {
+      float xr[V], xi[V];
+      load_vals<V, E>(base + t * a.row_stride, xr);
+      load_vals<V, E>(base + t * a.row_stride + a.F, xi);
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        re[j] += xr[j];
+        im[j] += xi[j];
+        ab[j] += sqrtf(xr[j] * xr[j] + xi[j] * xi[j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      out[j] = re[j];
+      out[V + j] = im[j];
+      out[2 * V + j] = ab[j];
+    }
+  } else {
+    const int c = col - a.rope_cols;
+    const int per = a.P / V;
+    const int h = c / per, p = (c % per) * V;
+    const uint16_t* base = a.q + (int64_t)h * a.D + 2 * a.F + p;
+    float s[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) s[j] = 0.f;
+    for (int64_t t = t0; t < t1; ++t) {
+      float x[V];
+      load_vals<V, E>(base + t * a.row_stride, x);
+#pragma unroll
+      for (int j = 0; j < V; ++j) s[j] += x[j];
+    }
+#pragma unroll
+    for (int j = 0; j < V; ++j) out[j] = s[j];
+  }
+}
+
+// out element e of kind k (0 re, 1 im, 2 abs, 3 pass) <- sum over chunks
+__global__ void __launch_bounds__(256) calib_finalize_kernel(const double* __restrict__ ws, int64_t nchunk, int cols,
+                                                             int rope_cols, int H, int F, int P, int V,
+                                                             double* re_sum, double* im_sum, double* abs_sum,
+                                                             double* pass_sum) {
+  const int64_t rope_elems = (int64_t)H * F;
+  const int64_t total = 3 * rope_elems + (int64_t)H * P;
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= total) return;
+  int col, slot;
+  double* dst;
+  if (e < 3 * rope_elems) {
+    const int kind = (int)(e / rope_elems);
+    const int64_t i = e % rope_elems;  // h*F + f
+    const int h = (int)(i / F), f = (int)(i % F);
+    col = h * (F / V) + f / V;
+    slot = kind * V + f % V;
+    dst = (kind == 0 ? re_sum : kind == 1 ? im_sum : abs_sum) + i;
+  } else {
+    const int64_t i = e - 3 * rope_elems;  // h*P + p
+    const int h = (int)(i / P), p = (int)(i % P);
+    col = rope_cols + h * (P / V) + p / V;
+    slot = p % V;
+    dst = pass_sum + i;
+  }
+  double acc = 0.0;
+  for (int64_t c = 0; c < nchunk; ++c) acc += ws[((int64_t)c * cols + col) * 3 * V + slot];
+  *dst += acc;
+}
+
+inline int calib_vec(int F, int P, int64_t row_stride, const void* q) {
+  if (F % 8 == 0 && P % 8 == 0 && row_stride % 8 == 0 && aligned(q, 16)) return 8;
+  if (F % 2 == 0 && P % 2 == 0 && row_stride % 2 == 0 && aligned(q, 4)) return 2;
+  return 1;
+}
+
+}  // namespace kvc
+
+using namespace kvc;
+
+extern "C" int64_t kvc_calibration_workspace_doubles(int64_t n_tokens, int heads, int head_dim, int rotary_dim) {
+  if (n_tokens <= 0 || heads <= 0 || head_dim <= 0 || rotary_dim <= 0 || rotary_dim > head_dim) return 0;
+  const int F = rotary_dim / 2, P = head_dim - rotary_dim;
+  // upper bound over vector widths: one column per element at V = 1
+  const int64_t cols_v1 = (int64_t)heads * (F + P);
+  const int64_t nchunk = (n_tokens + kCalibChunk - 1) / kCalibChunk;
+  return nchunk * cols_v1 * 3;
+}
+
+extern "C" int kvc_calibration_accumulate(const void* q, int dtype, int64_t n_tokens, int64_t row_stride, int heads,
+                                          int head_dim, int rotary_dim, double* re_sum, double* im_sum,
+                                          double* abs_sum, double* pass_sum, double* workspace,
+                                          int64_t workspace_doubles, void* stream) {
+  KVC_CHECK_ARG(q && re_sum && im_sum && abs_sum && workspace, KVC_ENULL);
+  KVC_CHECK_ARG(dtype == KVC_BF16 || dtype == KVC_FP16, KVC_EINVAL);
+  KVC_CHECK_ARG(n_tokens >= 0 && heads > 0 && head_dim > 0 && rotary_dim > 0 && rotary_dim <= head_dim &&
+                    rotary_dim % 2 == 0 && row_stride >= (int64_t)heads * head_dim,
+                KVC_EINVAL);
+  const int F = rotary_dim / 2, P = head_dim - rotary_dim;
+  KVC_CHECK_ARG(P == 0 || pass_sum != nullptr, KVC_ENULL);
+  KVC_CHECK_ARG(aligned(q, 2), KVC_EALIGN);
+  if (n_tokens == 0) return KVC_OK;
+  KVC_CHECK_ARG(workspace_doubles >= kvc_calibration_workspace_doubles(n_tokens, heads, head_dim, rotary_dim),
+                KVC_EINVAL);
+  const int V = calib_vec(F, P, row_stride, q);
+  CalibArgs a{};
+  a.q = (const uint16_t*)q;
+  a.n_tok = n_tokens;
+  a.row_stride = row_stride;
+  a.H = heads;
+  a.D = head_dim;
+  a.F = F;
+  a.P = P;
+  a.V = V;
+  a.rope_cols = heads * (F / V);
+  a.cols = a.rope_cols + heads * (P / V);
+  a.ws = workspace;
+  const int64_t nchunk = (n_tokens + kCalibChunk - 1) / kCalibChunk;
+  KVC_CHECK_ARG(nchunk <= 65535, KVC_EINVAL);
+  const dim3 grid((a.cols + kCalibThreads - 1) / kCalibThreads, (unsigned)nchunk);
+  cudaStream_t st = (cudaStream_t)stream;
+#define KVC_CALIB(VV, EE) calib_partial_kernel<VV, EE><<<grid, kCalibThreads, 0, st>>>(a)
+  if (dtype == KVC_BF16) {
+    if (V == 8) KVC_CALIB(8, Bf16); else if (V == 2) KVC_CALIB(2, Bf16); else KVC_CALIB(1, Bf16);
+  } else {
+    if (V == 8) KVC_CALIB(8, Fp16); else if (V == 2) KVC_CALIB(2, Fp16); else KVC_CALIB(1, Fp16);
+  }
+#undef KVC_CALIB
+  int rc = launch_status();
+  if (rc != KVC_OK) return rc;
+  const int64_t total = 3LL * heads * F + (int64_t)heads * P;
+  calib_finalize_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
+      workspace, nchunk, a.cols, a.rope_cols, heads, F, P, V, re_sum, im_sum, abs_sum, pass_sum);
+  return launch_status();
+}

@@ -1,0 +1,309 @@
+// Paged K/V compaction, slot gather/scatter and decode position shift (sm_100a).
+//
+// Compaction moves N_layers * 2 * R * budget token rows (row = all local KV
+// heads of one token, contiguous in the [blocks][128][kvh][D] layout).  Each
+// warp owns a tile of 32 consecutive output rows: lane i resolves row i's
+// source/destination addresses (keep index -> source block -> address, with
+// range checks) so the dependent index loads of 32 rows overlap; the warp then
+// streams the rows with 16-byte vectors (narrower when the caller's strides or
+// bases are not 16-byte aligned), two rows in flight per pass.
+#include "kvc_common.cuh"
+
+namespace kvc {
+
+constexpr int kMaxCompactLayers = 512;
+constexpr int kCopyThreads = 256;
+
+struct CompactArgs {
+  const void* k_layers[kMaxCompactLayers];
+  const void* v_layers[kMaxCompactLayers];
+  int64_t block_stride;  // bytes
+  int64_t num_blocks;
+  int64_t row_bytes;
+  const int64_t* src_blocks;
+  const int64_t* src_block_off;
+  const int64_t* dst_blocks;
+  const int64_t* dst_block_off;
+  const int64_t* keep;
+  const int32_t* tokens;
+  int32_t* error_flag;
+  int N, R, budget;
+};
+
+template <int VEC>
+struct Vec;
+template <> struct Vec<16> { using T = uint4; };
+template <> struct Vec<8> { using T = uint2; };
+template <> struct Vec<4> { using T = uint32_t; };
+template <> struct Vec<2> { using T = uint16_t; };
+
+template <int VEC>
+__device__ __forceinline__ typename Vec<VEC>::T load_nc(const void* p) {
+  using T = typename Vec<VEC>::T;
+  if constexpr (VEC == 16) return ldg_stream16(p);
+  else return __ldg(reinterpret_cast<const T*>(p));
+}
+
+// Resolve (src, dst) byte addresses of output row q; nullptr on a range fault.
+__device__ __forceinline__ void resolve_row(const CompactArgs& a, int64_t q, const char*& src, char*& dst) {
+  src = nullptr;
+  dst = nullptr;
+  const int64_t j = q % a.budget;
+  int64_t t = q / a.budget;
+  const int r = (int)(t % a.R);
+  t /= a.R;
+  const int kv = (int)(t & 1);
+  const int layer = (int)(t >> 1);
+  const int64_t idx = __ldg(a.keep + (int64_t)r * a.budget + j);
+  if (idx < 0 || idx >= __ldg(a.tokens + r)) {
+    raise_flag(a.error_flag, KVC_DEV_TOKEN_RANGE);
+    return;
+  }
+  const int64_t sb = __ldg(a.src_blocks + __ldg(a.src_block_off + r) + (idx >> 7));
+  const int64_t db = __ldg(a.dst_blocks + __ldg(a.dst_block_off + r) + (j >> 7));
+  if (sb < 0 || sb >= a.num_blocks || db < 0 || db >= a.num_blocks) {
+    raise_flag(a.error_flag, KVC_DEV_BLOCK_RANGE);
+    return;
+  }
+  const char* base_s = reinterpret_cast<const char*>(kv ? a.v_layers[layer] : a.k_layers[layer]);
+  char* base_d = const_cast<char*>(base_s);
+  src = base_s + sb * a.block_stride + (idx & 127) * a.row_bytes;
+  dst = base_d + db * a.block_stride + (j & 127) * a.row_bytes;
+}
+
+template <int VEC>
+__global__ void __launch_bounds__(kCopyThreads) compact_kernel(const __grid_constant__ CompactArgs a) {
+  using T = typename Vec<VEC>::T;
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = (int64_t)a.N * 2 * a.R * a.budget;
+  const int64_t tiles = (rows + 31) / 32;
+  const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int nvec = (int)(a.row_bytes / VEC);
+  for (int64_t tile = warp0; tile < tiles; tile += nwarps) {
+    const int64_t q = tile * 32 + lane;
+    const char* my_src = nullptr;
+    char* my_dst = nullptr;
+    if (q < rows) resolve_row(a, q, my_src, my_dst);
+    const int nrows = (int)min64(32, rows - tile * 32);
+    for (int k = 0; k < nrows; k += 2) {
+      const char* s0 = (const char*)__shfl_sync(0xffffffffu, (unsigned long long)my_src, k);
+      char* d0 = (char*)__shfl_sync(0xffffffffu, (unsigned long long)my_dst, k);
+      const int k1 = min(k + 1, nrows - 1);
+      const char* s1 = (const char*)__shfl_sync(0xffffffffu, (unsigned long long)my_src, k1);
+      char* d1 = (char*)__shfl_sync(0xffffffffu, (unsigned long long)my_dst, k1);
+      if (k1 == k) { s1 = nullptr; d1 = nullptr; }
+      for (int v0 = 0; v0 < nvec; v0 += 32 * 4) {
+        T x0[4], x1[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int v = v0 + u * 32 + lane;
+          if (v < nvec) {
+            if (s0) x0[u] = load_nc<VEC>(s0 + (int64_t)v * VEC);
+            if (s1) x1[u] = load_nc<VEC>(s1 + (int64_t)v * VEC);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int v = v0 + u * 32 + lane;
+          if (v < nvec) {
+            if (s0) *reinterpret_cast<T*>(d0 + (int64_t)v * VEC) = x0[u];
+            if (s1) *reinterpret_cast<T*>(d1 + (int64_t)v * VEC) = x1[u];
+          }
+        }
+      }
+    }
+  }
+}
+
+__global__ void stage_commit_kernel(const int64_t* __restrict__ dst_blocks, const int64_t* __restrict__ dst_block_off,
+                                    int R, int64_t* staged_rows, int stride, int64_t* staged_offsets,
+                                    const int64_t* __restrict__ semantic, int budget) {
+  const int r = blockIdx.x;
+  const int64_t b0 = dst_block_off[r], b1 = dst_block_off[r + 1];
+  if (staged_rows)
+    for (int64_t i = threadIdx.x; i < stride; i += blockDim.x)
+      staged_rows[(int64_t)r * stride + i] = (b0 + i < b1) ? dst_blocks[b0 + i] : -1;
+  if (staged_offsets && semantic && threadIdx.x == 0) staged_offsets[r] = semantic[r] - budget;
+}
+
+// ---- slot gather / scatter (workspace path of the cache API) -------------
+
+template <int VEC, bool GATHER>
+__global__ void __launch_bounds__(kCopyThreads) slots_kernel(const char* cache_in, char* cache_out,
+                                                             int64_t block_stride, int block_size,
+                                                             int64_t num_blocks, int64_t row_bytes,
+                                                             const int64_t* __restrict__ slots, int64_t n,
+                                                             const char* ws_in, char* ws_out, int32_t* flag) {
+  using T = typename Vec<VEC>::T;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int nvec = (int)(row_bytes / VEC);
+  for (int64_t i = warp0; i < n; i += nwarps) {
+    const int64_t slot = __ldg(slots + i);
+    const int64_t blk = slot / block_size;
+    if (slot < 0 || blk >= num_blocks) {
+      if (lane == 0) raise_flag(flag, KVC_DEV_BLOCK_RANGE);
+      continue;
+    }
+    const int64_t off = blk * block_stride + (slot % block_size) * row_bytes;
+    for (int v = lane; v < nvec; v += 32) {
+      if (GATHER)
+        *reinterpret_cast<T*>(ws_out + i * row_bytes + (int64_t)v * VEC) =
+            *reinterpret_cast<const T*>(cache_in + off + (int64_t)v * VEC);
+      else
+        *reinterpret_cast<T*>(cache_out + off + (int64_t)v * VEC) =
+            *reinterpret_cast<const T*>(ws_in + i * row_bytes + (int64_t)v * VEC);
+    }
+  }
+}
+
+template <typename I>
+__global__ void shift_positions_kernel(const int64_t* __restrict__ pos, const I* __restrict__ req,
+                                       const int64_t* __restrict__ offsets, int64_t num_offsets, int64_t n,
+                                       int64_t* out, int32_t* flag) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int64_t r = (int64_t)req[i];
+  if (r < 0 || r >= num_offsets) {
+    raise_flag(flag, KVC_DEV_BLOCK_RANGE);
+    out[i] = pos[i];
+    return;
+  }
+  out[i] = pos[i] - offsets[r];
+}
+
+inline int vec_width(uintptr_t bits) {
+  if (bits % 16 == 0) return 16;
+  if (bits % 8 == 0) return 8;
+  if (bits % 4 == 0) return 4;
+  if (bits % 2 == 0) return 2;
+  return 0;
+}
+
+inline unsigned copy_grid(int64_t work_warps) {
+  const int64_t cap = (int64_t)sm_count() * (2048 / kCopyThreads);
+  const int64_t want = (work_warps * 32 + kCopyThreads - 1) / kCopyThreads;
+  return (unsigned)std::max<int64_t>(1, std::min(cap, want));
+}
+
+}  // namespace kvc
+
+using namespace kvc;
+
+extern "C" int kvc_compact(const void* const* k_layers, const void* const* v_layers, int N,
+                           int64_t block_stride_bytes, int64_t num_blocks, int64_t row_bytes,
+                           const int64_t* src_blocks, const int64_t* src_block_off, const int64_t* dst_blocks,
+                           const int64_t* dst_block_off, const int64_t* keep, const int32_t* tokens, int R,
+                           int budget, int64_t* staged_rows, int staged_row_stride, int64_t* staged_offsets,
+                           const int64_t* semantic, int32_t* error_flag, void* stream) {
+  KVC_CHECK_ARG(k_layers && v_layers && src_blocks && src_block_off && dst_blocks && dst_block_off && keep && tokens,
+                KVC_ENULL);
+  KVC_CHECK_ARG(N > 0 && R >= 0 && budget > 0 && row_bytes > 0 && num_blocks > 0, KVC_EINVAL);
+  KVC_CHECK_ARG(block_stride_bytes >= (int64_t)kBlock * row_bytes, KVC_EINVAL);
+  KVC_CHECK_ARG(staged_rows == nullptr || staged_row_stride > 0, KVC_EINVAL);
+  if (R == 0) return KVC_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  uintptr_t bits = (uintptr_t)block_stride_bytes | (uintptr_t)row_bytes;
+  for (int i = 0; i < N; ++i) {
+    KVC_CHECK_ARG(k_layers[i] && v_layers[i], KVC_ENULL);
+    bits |= (uintptr_t)k_layers[i] | (uintptr_t)v_layers[i];
+  }
+  const int vec = vec_width(bits);
+  KVC_CHECK_ARG(vec > 0, KVC_EALIGN);
+  for (int l0 = 0; l0 < N; l0 += kMaxCompactLayers) {
+    CompactArgs a{};
+    a.N = std::min(kMaxCompactLayers, N - l0);
+    for (int i = 0; i < a.N; ++i) {
+      a.k_layers[i] = k_layers[l0 + i];
+      a.v_layers[i] = v_layers[l0 + i];
+    }
+    a.block_stride = block_stride_bytes;
+    a.num_blocks = num_blocks;
+    a.row_bytes = row_bytes;
+    a.src_blocks = src_blocks;
+    a.src_block_off = src_block_off;
+    a.dst_blocks = dst_blocks;
+    a.dst_block_off = dst_block_off;
+    a.keep = keep;
+    a.tokens = tokens;
+    a.error_flag = error_flag;
+    a.R = R;
+    a.budget = budget;
+    const int64_t rows = (int64_t)a.N * 2 * R * budget;
+    const unsigned grid = copy_grid((rows + 31) / 32);
+    switch (vec) {
+      case 16: compact_kernel<16><<<grid, kCopyThreads, 0, st>>>(a); break;
+      case 8: compact_kernel<8><<<grid, kCopyThreads, 0, st>>>(a); break;
+      case 4: compact_kernel<4><<<grid, kCopyThreads, 0, st>>>(a); break;
+      default: compact_kernel<2><<<grid, kCopyThreads, 0, st>>>(a); break;
+    }
+    const int rc = launch_status();
+    if (rc != KVC_OK) return rc;
+  }
+  if (staged_rows || (staged_offsets && semantic)) {
+    stage_commit_kernel<<<R, 128, 0, st>>>(dst_blocks, dst_block_off, R, staged_rows, staged_row_stride,
+                                           staged_offsets, semantic, budget);
+    return launch_status();
+  }
+  return KVC_OK;
+}
+
+template <bool GATHER>
+static int slots_launch(const void* cache_in, void* cache_out, int64_t block_stride_bytes, int block_size,
+                        int64_t num_blocks, int64_t row_bytes, const int64_t* slots, int64_t n, const void* ws_in,
+                        void* ws_out, int32_t* flag, void* stream) {
+  KVC_CHECK_ARG(slots && (GATHER ? (cache_in && ws_out) : (cache_out && ws_in)), KVC_ENULL);
+  KVC_CHECK_ARG(block_size > 0 && num_blocks > 0 && row_bytes > 0 && n >= 0, KVC_EINVAL);
+  KVC_CHECK_ARG(block_stride_bytes >= (int64_t)block_size * row_bytes, KVC_EINVAL);
+  if (n == 0) return KVC_OK;
+  const uintptr_t bits = (uintptr_t)block_stride_bytes | (uintptr_t)row_bytes |
+                         (uintptr_t)(GATHER ? cache_in : cache_out) | (uintptr_t)(GATHER ? ws_out : ws_in);
+  const int vec = vec_width(bits);
+  KVC_CHECK_ARG(vec > 0, KVC_EALIGN);
+  const unsigned grid = copy_grid(n);
+  cudaStream_t st = (cudaStream_t)stream;
+  const char* ci = (const char*)cache_in;
+  char* co = (char*)cache_out;
+  const char* wi = (const char*)ws_in;
+  char* wo = (char*)ws_out;
+  switch (vec) {
+    case 16: slots_kernel<16, GATHER><<<grid, kCopyThreads, 0, st>>>(ci, co, block_stride_bytes, block_size, num_blocks, row_bytes, slots, n, wi, wo, flag); break;
+    case 8: slots_kernel<8, GATHER><<<grid, kCopyThreads, 0, st>>>(ci, co, block_stride_bytes, block_size, num_blocks, row_bytes, slots, n, wi, wo, flag); break;
+    case 4: slots_kernel<4, GATHER><<<grid, kCopyThreads, 0, st>>>(ci, co, block_stride_bytes, block_size, num_blocks, row_bytes, slots, n, wi, wo, flag); break;
+    default: slots_kernel<2, GATHER><<<grid, kCopyThreads, 0, st>>>(ci, co, block_stride_bytes, block_size, num_blocks, row_bytes, slots, n, wi, wo, flag); break;
+  }
+  return launch_status();
+}
+
+extern "C" int kvc_gather_slots(const void* cache, int64_t block_stride_bytes, int block_size, int64_t num_blocks,
+                                int64_t row_bytes, const int64_t* slots, int64_t n, void* out, int32_t* error_flag,
+                                void* stream) {
+  return slots_launch<true>(cache, nullptr, block_stride_bytes, block_size, num_blocks, row_bytes, slots, n,
+                            nullptr, out, error_flag, stream);
+}
+
+extern "C" int kvc_scatter_slots(void* cache, int64_t block_stride_bytes, int block_size, int64_t num_blocks,
+                                 int64_t row_bytes, const int64_t* slots, int64_t n, const void* in,
+                                 int32_t* error_flag, void* stream) {
+  return slots_launch<false>(nullptr, cache, block_stride_bytes, block_size, num_blocks, row_bytes, slots, n, in,
+                             nullptr, error_flag, stream);
+}
+
+extern "C" int kvc_shift_positions(const int64_t* positions, const void* request_indices, int index_bytes,
+                                   const int64_t* offsets, int64_t num_offsets, int64_t n, int64_t* out,
+                                   int32_t* error_flag, void* stream) {
+  KVC_CHECK_ARG(positions && request_indices && offsets && out, KVC_ENULL);
+  KVC_CHECK_ARG((index_bytes == 4 || index_bytes == 8) && n >= 0 && num_offsets >= 0, KVC_EINVAL);
+  if (n == 0) return KVC_OK;
+  const unsigned grid = (unsigned)((n + 255) / 256);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (index_bytes == 4)
+    shift_positions_kernel<int32_t><<<grid, 256, 0, st>>>(positions, (const int32_t*)request_indices, offsets,
+                                                          num_offsets, n, out, error_flag);
+  else
+    shift_positions_kernel<int64_t><<<grid, 256, 0, st>>>(positions, (const int64_t*)request_indices, offsets,
+                                                          num_offsets, n, out, error_flag);
+  return launch_status();
+}

@@ -1,0 +1,228 @@
+"""Torch-facing wrappers of the sm_100a TriAttention kernels (C ABI in include/kvc.h).
+
+Each wrapper checks that its tensors live on a CUDA device with the expected
+dtype and layout, passes raw pointers and the current CUDA stream to
+``libkvc_b200.so`` and raises RuntimeError on a non-zero status.  There is no
+CPU or torch fallback: a non-CUDA tensor is an error.
+
+Correspondence with the reference's device-op layer
+(src/vllm_ascend_kvcompress/methods/triattention/kernels.py and the torch ops
+of selection.py / cache.py / method.py):
+
+=============================  =====================================================
+this module                    reference
+=============================  =====================================================
+prepare_score_coefficients     prepare_mean_phase_coefficients (kernels.py:85-122),
+                               phase formation of score_post_rope_keys (scoring.py:77-83)
+score_paged_keys               score_paged_keys_mean_precomputed (kernels.py:247-317)
+head_stats                     torch.var_mean(..., correction=0) (method.py:379,423)
+normalize_aggregate            aggregate_normalized_scores (kernels.py:407-437),
+                               _aggregate_torch (method.py:477-503), method.py:463-467
+aggregate_rows                 method.py:458-467 after the TP all-reduce
+select_keep                    select_keep_indices (selection.py:108-196)
+compact                        materialize_token_slots per layer (method.py:272-288)
+gather_slots / scatter_slots   _gather_slots / _write_slots (cache.py:18-45)
+calibration_accumulate         _LayerAccumulator.add (calibration.py:95-131)
+shift_positions                shift_positions (kernels.py:35-47)
+=============================  =====================================================
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from ... import _native as N
+
+BLOCK = 128
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _p(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def require_cuda(*tensors: torch.Tensor | None) -> None:
+    for t in tensors:
+        if t is not None and t.device.type != "cuda":
+            raise RuntimeError("the B200 TriAttention kernels require CUDA tensors (no CPU fallback)")
+
+
+def _dtype_code(dtype: torch.dtype) -> int:
+    if dtype == torch.bfloat16:
+        return N.BF16
+    if dtype == torch.float16:
+        return N.FP16
+    raise RuntimeError(f"unsupported KV/query dtype {dtype}; expected bfloat16 or float16")
+
+
+def _need(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
+    if t.dtype != dtype or not t.is_contiguous():
+        raise RuntimeError(f"{name} must be a contiguous {dtype} tensor")
+
+
+@dataclass
+class BatchPlan:
+    """Device metadata of one ragged batch (page-padded token space).
+
+    tokens [R] int32, page_off [R+1] int32, src_blocks/dst_blocks int64 CSR with
+    src_off/dst_off [R+1] int64, round_start and semantic [R] int64.
+    """
+
+    num_requests: int
+    total_pages: int
+    tokens: torch.Tensor
+    page_off: torch.Tensor
+    src_blocks: torch.Tensor
+    src_off: torch.Tensor
+    dst_blocks: torch.Tensor
+    dst_off: torch.Tensor
+    round_start: torch.Tensor
+    semantic: torch.Tensor
+    tokens_host: tuple[int, ...]
+    max_dst_blocks: int
+
+    @property
+    def tok_total(self) -> int:
+        return self.total_pages * BLOCK
+
+
+def coef_floats(num_freq: int, group: int, n_off: int, aggregation: int) -> int:
+    return int(N.lib().kvc_coef_floats(num_freq, group, n_off, aggregation))
+
+
+def prepare_score_coefficients(omega, offsets, plan: BatchPlan, q_real, q_imag, scale, extra, aggregation: int,
+                               coef_out) -> None:
+    require_cuda(omega, offsets, q_real, coef_out)
+    L, kvh, G, F = q_real.shape
+    for t, n in ((omega, "omega"), (offsets, "offsets"), (q_real, "q_real"), (q_imag, "q_imag"),
+                 (scale, "scale"), (extra, "extra"), (coef_out, "coef")):
+        _need(t, torch.float32, n)
+    N.check(N.lib().kvc_prepare_score_coefficients(
+        _p(omega), _p(offsets), offsets.numel(), _p(plan.round_start), plan.num_requests, L, kvh, G, F,
+        _p(q_real), _p(q_imag), _p(scale), _p(extra), aggregation, _p(coef_out), _stream()),
+        "kvc_prepare_score_coefficients")
+
+
+def score_paged_keys(k_ptrs, dtype: torch.dtype, block_stride: int, num_blocks: int, kvh: int, group: int,
+                     head_dim: int, rotary_dim: int, plan: BatchPlan, coef, n_off: int, aggregation: int,
+                     q_pass_t, raw_out, partial_out, error_flag) -> None:
+    N.check(N.lib().kvc_score_paged_keys(
+        k_ptrs, len(k_ptrs), _dtype_code(dtype), block_stride, num_blocks, kvh, group, head_dim, rotary_dim,
+        _p(plan.src_blocks), _p(plan.src_off), _p(plan.tokens), _p(plan.page_off), plan.num_requests,
+        plan.total_pages, _p(coef), n_off, aggregation, _p(q_pass_t), _p(raw_out), _p(partial_out),
+        _p(error_flag), _stream()), "kvc_score_paged_keys")
+
+
+def head_stats(partial, num_layers: int, heads: int, plan: BatchPlan, mean_out, var_out, den_out) -> None:
+    N.check(N.lib().kvc_head_stats(
+        _p(partial), num_layers, plan.num_requests, plan.total_pages, heads, _p(plan.tokens), _p(plan.page_off),
+        _p(mean_out), _p(var_out), _p(den_out), _stream()), "kvc_head_stats")
+
+
+def normalize_aggregate(raw, num_layers: int, heads: int, plan: BatchPlan, mean, den, layer_aggregation: int,
+                        rows_out=None, agg_out=None) -> None:
+    N.check(N.lib().kvc_normalize_aggregate(
+        _p(raw), num_layers, heads, plan.total_pages, _p(mean), _p(den), _p(plan.tokens), _p(plan.page_off),
+        plan.num_requests, layer_aggregation, _p(rows_out), _p(agg_out), _stream()), "kvc_normalize_aggregate")
+
+
+def aggregate_rows(rows, num_layers: int, plan: BatchPlan, layer_aggregation: int, agg_out) -> None:
+    N.check(N.lib().kvc_aggregate_rows(
+        _p(rows), num_layers, plan.total_pages, _p(plan.tokens), _p(plan.page_off), plan.num_requests,
+        layer_aggregation, _p(agg_out), _stream()), "kvc_aggregate_rows")
+
+
+def select_keep(agg, plan: BatchPlan, budget: int, prefix: int, recent: int, segments: int, policy: int,
+                keep_out, error_flag) -> None:
+    require_cuda(agg, keep_out)
+    N.check(N.lib().kvc_select_keep(
+        _p(agg), _p(plan.tokens), _p(plan.page_off), plan.num_requests, budget, prefix, recent, segments, policy,
+        _p(keep_out), _p(error_flag), _stream()), "kvc_select_keep")
+
+
+def compact(k_ptrs, v_ptrs, block_stride_bytes: int, num_blocks: int, row_bytes: int, plan: BatchPlan, keep,
+            budget: int, error_flag, staged_rows=None, staged_offsets=None) -> None:
+    N.check(N.lib().kvc_compact(
+        k_ptrs, v_ptrs, len(k_ptrs), block_stride_bytes, num_blocks, row_bytes, _p(plan.src_blocks),
+        _p(plan.src_off), _p(plan.dst_blocks), _p(plan.dst_off), _p(keep), _p(plan.tokens), plan.num_requests,
+        budget, _p(staged_rows), 0 if staged_rows is None else staged_rows.shape[1], _p(staged_offsets),
+        _p(plan.semantic), _p(error_flag), _stream()), "kvc_compact")
+
+
+def _cache_geometry(cache: torch.Tensor) -> tuple[int, int, int]:
+    """(block stride bytes, block size, row bytes) of a [blocks, bs, heads, dim] cache."""
+    if cache.ndim != 4:
+        raise ValueError("cache must use [blocks, block, heads, dim] layout")
+    _, bs, h, d = cache.shape
+    es = cache.element_size()
+    if cache.stride()[1:] != (h * d, d, 1):
+        raise RuntimeError("cache inner dims must be contiguous")
+    return cache.stride(0) * es, bs, h * d * es
+
+
+def gather_slots(cache: torch.Tensor, slots: torch.Tensor, out: torch.Tensor | None = None,
+                 error_flag: torch.Tensor | None = None) -> torch.Tensor:
+    """``out[i] = cache.view(-1, heads, dim)[slots[i]]`` for any page stride."""
+    require_cuda(cache, slots)
+    stride_b, bs, row_b = _cache_geometry(cache)
+    n = slots.numel()
+    if out is None:
+        out = torch.empty((n, cache.shape[2], cache.shape[3]), dtype=cache.dtype, device=cache.device)
+    _need(slots, torch.int64, "slots")
+    if out.dtype != cache.dtype or not out.is_contiguous() or out.numel() * out.element_size() < n * row_b:
+        raise RuntimeError("gather output must be a contiguous tensor of the cache dtype and row count")
+    N.check(N.lib().kvc_gather_slots(_p(cache), stride_b, bs, cache.shape[0], row_b, _p(slots), n, _p(out),
+                                     _p(error_flag), _stream()), "kvc_gather_slots")
+    return out
+
+
+def scatter_slots(cache: torch.Tensor, slots: torch.Tensor, values: torch.Tensor,
+                  error_flag: torch.Tensor | None = None) -> None:
+    """``cache.view(-1, heads, dim)[slots[i]] = values[i]`` for any page stride."""
+    require_cuda(cache, slots, values)
+    stride_b, bs, row_b = _cache_geometry(cache)
+    _need(slots, torch.int64, "slots")
+    if values.dtype != cache.dtype or not values.is_contiguous():
+        raise RuntimeError("scatter values must be a contiguous tensor of the cache dtype")
+    N.check(N.lib().kvc_scatter_slots(_p(cache), stride_b, bs, cache.shape[0], row_b, _p(slots), slots.numel(),
+                                      _p(values), _p(error_flag), _stream()), "kvc_scatter_slots")
+
+
+def calibration_workspace_doubles(n_tokens: int, heads: int, head_dim: int, rotary_dim: int) -> int:
+    return int(N.lib().kvc_calibration_workspace_doubles(n_tokens, heads, head_dim, rotary_dim))
+
+
+def calibration_accumulate(q: torch.Tensor, heads: int, head_dim: int, rotary_dim: int, re_sum, im_sum,
+                           abs_sum, pass_sum, workspace) -> None:
+    """Add per-(head, frequency) sums of pre-RoPE queries ``q [tokens, >= heads*head_dim]``."""
+    require_cuda(q, re_sum, workspace)
+    if q.ndim != 2 or q.stride(1) != 1:
+        raise RuntimeError("calibration queries must be [tokens, width] with a contiguous last dim")
+    for t, n in ((re_sum, "re_sum"), (im_sum, "im_sum"), (abs_sum, "abs_sum"), (workspace, "workspace")):
+        _need(t, torch.float64, n)
+    N.check(N.lib().kvc_calibration_accumulate(
+        _p(q), _dtype_code(q.dtype), q.shape[0], q.stride(0), heads, head_dim, rotary_dim, _p(re_sum),
+        _p(im_sum), _p(abs_sum), _p(pass_sum), _p(workspace), workspace.numel(), _stream()),
+        "kvc_calibration_accumulate")
+
+
+def shift_positions(positions: torch.Tensor, request_indices: torch.Tensor, request_offsets: torch.Tensor,
+                    output: torch.Tensor, error_flag: torch.Tensor | None = None) -> torch.Tensor:
+    """``output = positions - request_offsets[request_indices]`` (reference kernels.py:35-47)."""
+    require_cuda(positions, request_indices, request_offsets, output)
+    for t, n in ((positions, "positions"), (request_offsets, "request_offsets"), (output, "output")):
+        _need(t, torch.int64, n)
+    if request_indices.dtype not in (torch.int32, torch.int64) or not request_indices.is_contiguous():
+        raise RuntimeError("request_indices must be a contiguous int32/int64 tensor")
+    if output.numel() != positions.numel() or request_indices.numel() != positions.numel():
+        raise ValueError("positions, request_indices and output must have the same length")
+    N.check(N.lib().kvc_shift_positions(
+        _p(positions), _p(request_indices), request_indices.element_size(), _p(request_offsets),
+        request_offsets.numel(), positions.numel(), _p(output), _p(error_flag), _stream()),
+        "kvc_shift_positions")
+    return output

@@ -1,0 +1,466 @@
+"""TriAttention token-selection method on B200: score -> select -> compact in CUDA.
+
+Public behaviour follows the reference method
+(src/vllm_ascend_kvcompress/methods/triattention/method.py:57-519): the same
+name, runtime spec, compatibility check, binding rules (target vs MTP layers,
+layer-index checks, TP head sharding of the statistics) and result.  The work
+differs in shape: a whole step's requests are processed by one launch per
+stage over a ragged, page-padded token space, instead of one torch op chain
+per request and per layer:
+
+    prepare coefficients -> score every page of every scoring layer -> per-head
+    moments -> normalise + head max (+ layer mean/max, or per-layer rows that
+    one NCCL MAX all-reduce synchronises across TP ranks) -> segmented select
+    -> one compaction launch for all layers and requests.
+
+``compress(request)`` is ``compress_many((request,))``; ``compress_many`` is an
+optional batched extension a provider may probe for.  All launches go to the
+current CUDA stream; nothing here synchronises with the host except the
+explicit ``check_device_errors``.
+"""
+
+from __future__ import annotations
+
+import os
+from collections.abc import Mapping, Sequence
+from dataclasses import dataclass
+from typing import Any
+
+import torch
+
+from ... import _native as N
+from ...config import ASCEND_BLOCK_SIZE, JsonScalar
+from ..base import (
+    CompressionRequest,
+    CompressionResult,
+    KVCompressionMethod,
+    LayerCache,
+    MethodRuntimeSpec,
+    ModelShape,
+)
+from . import kernels as K
+from .config import TriAttentionConfig
+from .scoring import build_geometric_offsets
+from .stats import CalibrationStats, DeviceLayerCalibrationStats
+
+METHOD_NAME = "triattention"
+_STRICT_ENV = "KVC_B200_STRICT"
+
+
+def _queries_per_kv_head(shape: ModelShape) -> int:
+    if shape.num_attention_heads % shape.num_kv_heads:
+        raise RuntimeError("TriAttention requires query heads divisible by KV heads")
+    return shape.num_attention_heads // shape.num_kv_heads
+
+
+def _is_mtp_cache_layer(layer_name: str) -> bool:
+    return ".mtp.layers." in f".{layer_name}."
+
+
+@dataclass(frozen=True)
+class TriAttentionLayerCache:
+    name: str
+    k_cache: torch.Tensor
+    v_cache: torch.Tensor
+    stats: DeviceLayerCalibrationStats
+    frequency_scale: torch.Tensor | None = None
+    extra_coefficient: torch.Tensor | None = None
+    offset_cos_mean: torch.Tensor | None = None
+    offset_sin_mean: torch.Tensor | None = None
+
+
+class _Workspaces:
+    """Method-owned device buffers, grown (never shrunk) to the largest batch seen."""
+
+    def __init__(self, device: torch.device) -> None:
+        self.device = device
+        self._bufs: dict[str, torch.Tensor] = {}
+
+    def get(self, name: str, numel: int, dtype: torch.dtype) -> torch.Tensor:
+        buf = self._bufs.get(name)
+        if buf is None or buf.numel() < numel or buf.dtype != dtype:
+            cap = max(numel, int(buf.numel() * 1.25) if buf is not None and buf.dtype == dtype else 0, 1)
+            buf = torch.empty(cap + 16, dtype=dtype, device=self.device)
+            self._bufs[name] = buf
+        return buf[:numel]
+
+
+class TriAttentionMethod(KVCompressionMethod):
+    """TriAttention KV compression with sm_100a kernels."""
+
+    def __init__(self, options: Mapping[str, JsonScalar], vllm_config: Any, model_shape: ModelShape) -> None:
+        self.config = TriAttentionConfig.from_method_config(options)
+        self.vllm_config = vllm_config
+        self.model_shape = model_shape
+        self.calibration = CalibrationStats.load(self.config.stats_path)
+        self.layer_caches: tuple[TriAttentionLayerCache, ...] = ()
+        self.materialization_caches: tuple[LayerCache, ...] = ()
+        self.cache_block_size = ASCEND_BLOCK_SIZE
+        self.offsets: torch.Tensor | None = None
+        self.tensor_parallel_size = 1
+        self.tensor_parallel_rank = 0
+        self.tp_group = None
+        self.staged_block_rows: torch.Tensor | None = None
+        self.staged_offsets: torch.Tensor | None = None
+        self.profiler = None  # optional object with .mark(name) (bench timing hooks)
+        self._ws: _Workspaces | None = None
+        self._err_host: torch.Tensor | None = None
+        self._err_event: torch.cuda.Event | None = None
+
+    # ---- method API v1 ------------------------------------------------------
+
+    @property
+    def name(self) -> str:
+        return METHOD_NAME
+
+    @property
+    def runtime_spec(self) -> MethodRuntimeSpec:
+        return MethodRuntimeSpec(
+            requires_private_destination=True,
+            compression_threshold_tokens=self.config.compression_threshold_tokens,
+            required_recompute_tokens=self.config.recompute_window,
+            max_physical_num_tokens=self.config.kv_budget,
+            min_output_tokens_for_compression=self.config.min_output_tokens_for_compression,
+        )
+
+    def compatibility_reasons(self, worker: Any) -> tuple[str, ...]:
+        del worker
+        return self.calibration.validate(self.model_shape)
+
+    def bind_model_runner(self, runner: Any, layer_caches: tuple[LayerCache, ...]) -> None:
+        device = torch.device(runner.device)
+        if device.type != "cuda":
+            raise RuntimeError("the B200 TriAttention method requires CUDA KV caches")
+        if device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        K.require_cuda(*(c.k_cache for c in layer_caches))
+        N.lib()  # fail at bind time if the native library is missing
+        self.tensor_parallel_size = int(self.vllm_config.parallel_config.tensor_parallel_size)
+        self.tensor_parallel_rank = 0
+        if self.tensor_parallel_size > 1:
+            self.tp_group, self.tensor_parallel_rank = self._resolve_tp_group(runner)
+        stats = self.calibration.to_device(
+            self.model_shape, device, tensor_parallel_rank=self.tensor_parallel_rank,
+            tensor_parallel_size=self.tensor_parallel_size)
+        self.offsets = build_geometric_offsets(int(self.vllm_config.model_config.max_model_len), device)
+        mtp = tuple(c for c in layer_caches if _is_mtp_cache_layer(c.name))
+        targets = tuple(c for c in layer_caches if not _is_mtp_cache_layer(c.name))
+        spec = getattr(self.vllm_config, "speculative_config", None)
+        if mtp and (len(mtp) != 1 or mtp[0].name != "mtp.layers.0.self_attn.attn"
+                    or getattr(spec, "method", None) != "mtp"
+                    or getattr(spec, "num_speculative_tokens", None) != 2):
+            raise RuntimeError("uncalibrated MTP cache requires Qwen3.5 MTP2")
+        if len(targets) != len(self.model_shape.full_attention_layer_indices):
+            raise RuntimeError("allocated full-attention layer count does not match calibration")
+        bound, seen = [], set()
+        for c in targets:
+            if c.layer_index not in stats:
+                raise RuntimeError(f"attention layer {c.name!r} resolves to invalid model layer index {c.layer_index}")
+            if c.layer_index in seen:
+                raise RuntimeError(f"multiple cache layers resolve to model layer index {c.layer_index}")
+            seen.add(c.layer_index)
+            st = stats[c.layer_index]
+            qmag = torch.sqrt(st.q_mean_real.square() + st.q_mean_imag.square() + 1e-8)
+            bound.append(TriAttentionLayerCache(
+                name=c.name, k_cache=c.k_cache, v_cache=c.v_cache, stats=st,
+                frequency_scale=torch.sqrt(st.freq_scale_sq), extra_coefficient=st.q_abs_mean - qmag))
+        if seen != set(self.model_shape.full_attention_layer_indices):
+            raise RuntimeError("allocated target full-attention layers do not match calibration: "
+                               f"allocated={sorted(seen)} expected={sorted(self.model_shape.full_attention_layer_indices)}")
+        self.layer_caches = tuple(bound)
+        self.materialization_caches = layer_caches
+        self._bind_geometry(device)
+        self._bind_scoring_tensors()
+        self._ws = _Workspaces(device)
+        self._err = torch.zeros(1, dtype=torch.int32, device=device)
+        self._err_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self._err_event = None
+
+    def compress(self, request: CompressionRequest) -> CompressionResult:
+        return self.compress_many((request,))[0]
+
+    # ---- batched extension ----------------------------------------------------
+
+    def compress_many(self, requests: Sequence[CompressionRequest], *, stage_commit: bool = False
+                      ) -> tuple[CompressionResult, ...]:
+        """Score, select and compact a whole step's requests with one launch per stage."""
+        reqs = tuple(requests)
+        if not reqs:
+            return ()
+        self._require_bound()
+        self._raise_pending_device_error()
+        plan = self._plan([(r.physical_num_tokens, r.semantic_num_tokens, r.source_block_ids_device,
+                            r.destination_block_ids_device) for r in reqs])
+        keep = self._score_and_select(plan)
+        self._compact(plan, keep, stage_commit)
+        self._arm_error_check()
+        if os.environ.get(_STRICT_ENV, "") == "1":
+            self.check_device_errors()
+        lengths = tuple((c.name, self.config.kv_budget) for c in self.materialization_caches)
+        return tuple(CompressionResult(physical_num_tokens=self.config.kv_budget,
+                                       per_layer_physical_num_tokens=lengths) for _ in reqs)
+
+    def select_many(self, requests: Sequence[CompressionRequest]) -> torch.Tensor:
+        """Keep indices ``[R, kv_budget]`` (int64, sorted per row) without compaction."""
+        reqs = tuple(requests)
+        self._require_bound()
+        plan = self._plan([(r.physical_num_tokens, r.semantic_num_tokens, r.source_block_ids_device,
+                            r.destination_block_ids_device) for r in reqs], need_destination=False)
+        return self._score_and_select(plan).view(len(reqs), self.config.kv_budget).clone()
+
+    def _select_keep_indices(self, source_block_ids: torch.Tensor, physical_num_tokens: int,
+                             round_start: int) -> torch.Tensor:
+        """Sorted keep positions of one request (the reference method's private hook)."""
+        self._require_bound()
+        plan = self._plan([(physical_num_tokens, round_start, source_block_ids, None)], need_destination=False)
+        return self._score_and_select(plan)[: self.config.kv_budget].clone()
+
+    def check_device_errors(self) -> None:
+        """Synchronise on the last launch and raise if a kernel reported a bad index."""
+        if self._ws is None:
+            return
+        torch.cuda.current_stream().synchronize()
+        bits = int(self._err.item())
+        self._err_event = None
+        self._err_host.zero_()
+        if bits:
+            self._err.zero_()
+            raise RuntimeError(self._describe_error(bits))
+
+    # ---- binding helpers ----------------------------------------------------
+
+    def _resolve_tp_group(self, runner: Any):
+        """TP group and rank: vLLM's, unless the runner carries ``kvc_tp_group``/``kvc_tp_rank``.
+
+        The override lets a host that does not initialise vLLM's parallel state
+        (a standalone engine, a benchmark) pass its own process group and rank.
+        """
+        group = getattr(runner, "kvc_tp_group", None)
+        rank = getattr(runner, "kvc_tp_rank", None)
+        if rank is not None:
+            return group, int(rank)
+        if group is not None:
+            import torch.distributed as dist
+
+            return group, dist.get_rank(group)
+        from vllm.distributed import get_tp_group
+
+        tp = get_tp_group()
+        return tp.device_group, int(tp.rank_in_group)
+
+    def _bind_geometry(self, device: torch.device) -> None:
+        caches = self.materialization_caches
+        k0 = self.layer_caches[0].k_cache
+        if k0.ndim != 4 or k0.shape[1] != ASCEND_BLOCK_SIZE:
+            raise RuntimeError("TriAttention requires 128-token kernel cache blocks")
+        self.cache_block_size = int(k0.shape[1])
+        nb, _, kvh, d = k0.shape
+        expected_kvh = self.model_shape.num_kv_heads // self.tensor_parallel_size
+        if kvh != expected_kvh:
+            raise RuntimeError("local KV-cache head count does not match tensor-parallel model shape: "
+                               f"expected {expected_kvh}, got {kvh}")
+        if k0.dtype not in (torch.bfloat16, torch.float16):
+            raise RuntimeError(f"unsupported KV cache dtype {k0.dtype}")
+        for c in caches:
+            for t in (c.k_cache, c.v_cache):
+                if t.device != device or t.dtype != k0.dtype:
+                    raise RuntimeError(f"layer {c.name!r} cache must be {k0.dtype} on {device}")
+                if tuple(t.shape) != tuple(k0.shape) or t.stride() != k0.stride():
+                    raise RuntimeError(f"layer {c.name!r} cache geometry differs from the first layer")
+                if t.stride()[1:] != (kvh * d, d, 1) or t.stride(0) < ASCEND_BLOCK_SIZE * kvh * d:
+                    raise RuntimeError(f"layer {c.name!r} cache must have contiguous inner blocks")
+        es = k0.element_size()
+        self.kv_dtype = k0.dtype
+        self.num_blocks = int(nb)
+        self.local_kv_heads = int(kvh)
+        self.head_dim = int(d)
+        self.block_stride = int(k0.stride(0))
+        self.block_stride_bytes = self.block_stride * es
+        self.row_bytes = kvh * d * es
+        self._k_all = N.pointer_array([c.k_cache.data_ptr() for c in caches])
+        self._v_all = N.pointer_array([c.v_cache.data_ptr() for c in caches])
+
+    def _bind_scoring_tensors(self) -> None:
+        layers = self.layer_caches[:: self.config.score_layer_stride]
+        self.scoring_layer_count = len(layers)
+        self._k_score = N.pointer_array([c.k_cache.data_ptr() for c in layers])
+        st0 = layers[0].stats
+        self.group = _queries_per_kv_head(self.model_shape)
+        self.rotary_dim = int(st0.rotary_dim or self.head_dim)
+        self.num_freq = self.rotary_dim // 2
+        self.pass_dim = self.head_dim - self.rotary_dim
+        if self.pass_dim and any(c.stats.q_pass_mean is None for c in layers):
+            raise RuntimeError("partial-RoPE scoring requires q_pass_mean")
+        if any(c.stats.rope_style != "half" for c in layers):
+            raise RuntimeError("the CUDA scorer supports the 'half' RoPE layout only")
+        stack = lambda f: torch.stack([f(c) for c in layers]).contiguous()
+        self.scoring_omega = stack(lambda c: c.stats.omega)
+        self.scoring_q_real = stack(lambda c: c.stats.q_mean_real)
+        self.scoring_q_imag = stack(lambda c: c.stats.q_mean_imag)
+        self.scoring_scale = stack(lambda c: c.frequency_scale)
+        self.scoring_extra = stack(lambda c: c.extra_coefficient)
+        # [L][kvh][P][G]: one unrotated dim's G coefficients are contiguous
+        self.scoring_q_pass_t = (stack(lambda c: c.stats.q_pass_mean).transpose(-1, -2).contiguous()
+                                 if self.pass_dim else None)
+        self.score_aggregation_code = N.AGG_MEAN if self.config.score_aggregation == "mean" else N.AGG_MAX
+        self.layer_aggregation_code = N.AGG_MEAN if self.config.layer_aggregation == "mean" else N.AGG_MAX
+        self.coef_block = K.coef_floats(self.num_freq, self.group, self.offsets.numel(), self.score_aggregation_code)
+
+    # ---- per-step pipeline ----------------------------------------------------
+
+    def _require_bound(self) -> None:
+        if self.offsets is None or not self.layer_caches or self._ws is None:
+            raise RuntimeError("TriAttention method is not bound to KV cache")
+
+    def _plan(self, items, need_destination: bool = True) -> K.BatchPlan:
+        """Validate a batch on the host and stage its metadata on the device."""
+        budget = self.config.kv_budget
+        bs = self.cache_block_size
+        dev = self.offsets.device
+        tokens, pages, sem, srcs, dsts = [], [], [], [], []
+        dst_need = -(-budget // bs)
+        for t, s, src, dst in items:
+            t, s = int(t), int(s)
+            if budget <= 0 or budget > t:
+                raise ValueError("budget must be in [1, token_count]")
+            n = -(-t // bs)
+            if src.numel() < n:
+                raise RuntimeError("source block table is shorter than the physical token count")
+            tokens.append(t)
+            pages.append(n)
+            sem.append(s)
+            srcs.append(src.reshape(-1)[:n])
+            if need_destination:
+                if dst is None or dst.numel() < dst_need:
+                    raise RuntimeError("destination block table is shorter than kv_budget")
+                dsts.append(dst.reshape(-1)[:dst_need])
+        R = len(tokens)
+        page_off = [0]
+        for n in pages:
+            page_off.append(page_off[-1] + n)
+        src_off = page_off
+        dst_off = [i * dst_need for i in range(R + 1)] if need_destination else [0] * (R + 1)
+        i32 = torch.tensor(tokens + page_off, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+        i64 = torch.tensor(src_off + dst_off + sem + sem, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+        cat = lambda xs: (xs[0] if len(xs) == 1 else torch.cat(xs)).to(device=dev, dtype=torch.int64)
+        src_blocks = cat(srcs)
+        dst_blocks = cat(dsts) if need_destination else src_blocks[:0]
+        return K.BatchPlan(
+            num_requests=R, total_pages=page_off[-1], tokens=i32[:R], page_off=i32[R:],
+            src_blocks=src_blocks, src_off=i64[: R + 1], dst_blocks=dst_blocks, dst_off=i64[R + 1: 2 * R + 2],
+            round_start=i64[2 * R + 2: 3 * R + 2], semantic=i64[3 * R + 2:], tokens_host=tuple(tokens),
+            max_dst_blocks=dst_need)
+
+    def _mark(self, name: str) -> None:
+        if self.profiler is not None:
+            self.profiler.mark(name)
+
+    def _score_and_select(self, plan: K.BatchPlan) -> torch.Tensor:
+        ws = self._ws
+        cfg = self.config
+        L = self.scoring_layer_count
+        heads = self.local_kv_heads * self.group
+        R, tok = plan.num_requests, plan.tok_total
+        coef = ws.get("coef", R * L * self.local_kv_heads * self.coef_block, torch.float32)
+        raw = ws.get("raw", L * heads * tok, torch.float32)
+        partial = ws.get("partial", L * plan.total_pages * heads * 2, torch.float32)
+        mean = ws.get("mean", L * R * heads, torch.float32)
+        var = ws.get("var", L * R * heads, torch.float32)
+        den = ws.get("den", L * R * heads, torch.float32)
+        agg = ws.get("agg", tok, torch.float32)
+        keep = ws.get("keep", R * cfg.kv_budget, torch.int64)
+        self._mark("prepare")
+        K.prepare_score_coefficients(self.scoring_omega, self.offsets, plan, self.scoring_q_real,
+                                     self.scoring_q_imag, self.scoring_scale, self.scoring_extra,
+                                     self.score_aggregation_code, coef)
+        self._mark("score")
+        K.score_paged_keys(self._k_score, self.kv_dtype, self.block_stride, self.num_blocks, self.local_kv_heads,
+                           self.group, self.head_dim, self.rotary_dim, plan, coef, self.offsets.numel(),
+                           self.score_aggregation_code, self.scoring_q_pass_t, raw, partial, self._err)
+        self._mark("head_stats")
+        K.head_stats(partial, L, heads, plan, mean, var, den)
+        self._mark("normalize")
+        if self.tensor_parallel_size > 1:
+            rows = ws.get("rows", L * tok, torch.float32)
+            K.normalize_aggregate(raw, L, heads, plan, mean, den, self.layer_aggregation_code, rows_out=rows)
+            self._mark("tp_sync")
+            self._tp_all_reduce_max(rows)
+            self._mark("aggregate_rows")
+            K.aggregate_rows(rows, L, plan, self.layer_aggregation_code, agg)
+        else:
+            K.normalize_aggregate(raw, L, heads, plan, mean, den, self.layer_aggregation_code, agg_out=agg)
+        self._mark("select")
+        policy = N.POLICY_V3 if cfg.position_policy == "v3" else N.POLICY_GLOBAL
+        K.select_keep(agg, plan, cfg.kv_budget, cfg.protected_prefix_window, cfg.protected_recent_window,
+                      cfg.position_segments, policy, keep, self._err)
+        self.last_stats = (raw, mean, var, agg)  # views of workspaces, for inspection/tests
+        return keep
+
+    def _tp_all_reduce_max(self, rows: torch.Tensor) -> None:
+        tp_score_sync(rows, self.tp_group)
+
+    def _compact(self, plan: K.BatchPlan, keep: torch.Tensor, stage_commit: bool) -> None:
+        staged_rows = staged_off = None
+        if stage_commit:
+            staged_rows = self._ws.get("staged_rows", plan.num_requests * plan.max_dst_blocks, torch.int64
+                                       ).view(plan.num_requests, plan.max_dst_blocks)
+            staged_off = self._ws.get("staged_off", plan.num_requests, torch.int64)
+        self._mark("compact")
+        K.compact(self._k_all, self._v_all, self.block_stride_bytes, self.num_blocks, self.row_bytes, plan, keep,
+                  self.config.kv_budget, self._err, staged_rows, staged_off)
+        self._mark("end")
+        self.staged_block_rows, self.staged_offsets = staged_rows, staged_off
+
+    # ---- device error reporting ---------------------------------------------
+
+    def _arm_error_check(self) -> None:
+        self._err_host.copy_(self._err, non_blocking=True)
+        self._err_event = torch.cuda.Event()
+        self._err_event.record()
+
+    def _raise_pending_device_error(self) -> None:
+        ev = self._err_event
+        if ev is not None and ev.query():
+            bits = int(self._err_host.item())
+            self._err_event = None
+            if bits:
+                self._err.zero_()
+                raise RuntimeError(self._describe_error(bits))
+
+    @staticmethod
+    def _describe_error(bits: int) -> str:
+        what = []
+        if bits & N.DEV_BLOCK_RANGE:
+            what.append("a block id outside the KV cache")
+        if bits & N.DEV_TOKEN_RANGE:
+            what.append("a keep index outside its request")
+        if bits & N.DEV_BUDGET:
+            what.append("a request shorter than kv_budget or its protected windows")
+        return "TriAttention kernels rejected " + ", ".join(what)
+
+
+def tp_score_sync(rows: torch.Tensor, group=None) -> None:
+    """Tensor-parallel score sync: one in-place MAX all-reduce of the per-layer rows.
+
+    ``rows`` holds every scoring layer's head-max row of every request of the
+    step (``[L_s, tokens]``), so a step issues one collective.  MAX commutes
+    with KV-head sharding, hence every rank ends with the TP=1 rows and selects
+    identical indices (reference method.py:447-461 issues the same MAX per
+    request).  ``group`` defaults to vLLM's tensor-parallel device group.
+    """
+    import torch.distributed as dist
+
+    if group is None:
+        from vllm.distributed import get_tp_group
+
+        group = get_tp_group().device_group
+    dist.all_reduce(rows, op=dist.ReduceOp.MAX, group=group)
+
+
+def create_triattention_method(options: Mapping[str, JsonScalar], vllm_config: Any,
+                               model_shape: ModelShape) -> KVCompressionMethod:
+    return TriAttentionMethod(options, vllm_config, model_shape)
+
+
+# Backward-compatible import name from the pre-registry layout.
+TriAttentionAscendConfig = TriAttentionConfig
