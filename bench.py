@@ -203,7 +203,7 @@ def reference_arm(args) -> None:
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    w = W.config1(stride=args.stride)
+    w = W.config1(stride=args.stride, num_seqs=args.seqs, num_layers=args.layers)
     seq = sorted(w.compressed(), key=lambda i: w.lengths[i])[len(w.compressed()) // 2]  # median-length sequence
     budget_s = 150.0
     t0 = time.perf_counter()
@@ -226,8 +226,9 @@ def reference_arm(args) -> None:
 def config_dict(w: W.Workload, world: int) -> dict:
     o = w.options
     return {
-        "workload": "config1: Qwen2.5-14B-shaped ragged batch, 48 layers, 40 q / 8 kv heads, head_dim 128, "
-                    "32 seqs U[4096,32768] (seed 1), kv_budget 4608, V3 prefix 128 / recent 512 / 8 segments",
+        "workload": f"config1: Qwen2.5-14B-shaped ragged batch, {w.geometry.num_layers} layers, 40 q / 8 kv heads, "
+                    f"head_dim 128, {len(w.lengths)} seqs U[4096,32768] (seed 1), kv_budget 4608, "
+                    "V3 prefix 128 / recent 512 / 8 segments",
         "global_batch": len(w.lengths), "compressed_sequences": len(w.compressed()),
         "compressed_tokens": w.total_compressed_tokens(), "layers": w.geometry.num_layers,
         "score_layer_stride": o.score_layer_stride, "kv_budget": o.kv_budget,
@@ -253,7 +254,7 @@ def b200_arm(args) -> None:
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
         group = dist.group.WORLD
-    w = W.config1(stride=args.stride)
+    w = W.config1(stride=args.stride, num_seqs=args.seqs, num_layers=args.layers)
     geo = w.geometry
     if geo.num_kv_heads % world:
         raise SystemExit(f"{geo.num_kv_heads} KV heads cannot be sharded over {world} ranks")
@@ -404,6 +405,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--stride", type=int, default=8, help="score_layer_stride (8 = default, 1 = every layer)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seqs", type=int, default=32, help="sequences (32 = config 1; smaller only for profiling)")
+    ap.add_argument("--layers", type=int, default=48, help="layers (48 = config 1; smaller only for profiling)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3

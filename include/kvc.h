@@ -43,6 +43,7 @@ extern "C" {
 #define KVC_DEV_BLOCK_RANGE 1   /* a block id outside [0, num_blocks) */
 #define KVC_DEV_TOKEN_RANGE 2   /* a keep index outside [0, tokens) */
 #define KVC_DEV_BUDGET 4        /* budget/windows impossible for a request */
+#define KVC_DEV_TIMEOUT 8       /* a bounded pipeline wait expired (the kernel gave up) */
 
 /* cache element types */
 #define KVC_BF16 0
@@ -105,15 +106,46 @@ int kvc_score_paged_keys(const void* const* k_layers, int num_layers, int dtype,
                          float* raw_out, float* partial_out, int32_t* error_flag, void* stream);
 
 /*
+ * Tensor-core scorer (same contract as kvc_score_paged_keys, mean aggregation):
+ * each (page, KV head) K tile is staged by TMA (cp.async.bulk.tensor, 128-byte
+ * swizzle) and contracted with mma.sync against hi/lo-split bf16 (or fp16)
+ * coefficient fragments.  Replaces score_paged_keys_mean_precomputed
+ * (methods/triattention/kernels.py:247-317) for the supported geometries
+ * (kvc_tc_supported: query group <= 8 and (rotary/2, head_dim - rotary) in
+ * {(64,0), (32,0), (32,192), (32,64), (64,128), (128,0)}).
+ *   key_maps     host array of num_layers 128-byte TMA descriptors from
+ *                kvc_encode_key_maps (built once per cache binding).
+ *   frag         kvc_prepare_score_fragments output.
+ *   partial_out  [L][total_pages*4][kvh*G][2]: moments per quarter page.
+ */
+int kvc_tc_supported(int group, int head_dim, int rotary_dim);
+int kvc_encode_key_maps(const void* const* k_layers, int num_layers, int dtype, int64_t block_stride,
+                        int64_t num_blocks, int kv_heads, int head_dim, void* maps_out);
+int64_t kvc_fragment_words(int num_freq, int pass_dim);
+int kvc_prepare_score_fragments(const float* omega, const float* offsets, int n_off,
+                                const int64_t* round_start, int num_requests, int num_layers,
+                                int kv_heads, int group, int num_freq, int pass_dim,
+                                const float* q_real, const float* q_imag, const float* scale,
+                                const float* extra, const float* q_pass, int dtype, uint32_t* frag_out,
+                                void* stream);
+int kvc_score_paged_keys_tc(const void* key_maps, int num_layers, int dtype, int64_t num_blocks,
+                            int kv_heads, int group, int head_dim, int rotary_dim,
+                            const int64_t* src_blocks, const int64_t* src_block_off,
+                            const int32_t* tokens, const int32_t* page_off, int num_requests,
+                            int total_pages, const uint32_t* frag, float* raw_out, float* partial_out,
+                            int32_t* error_flag, void* stream);
+
+/*
  * Per (scoring layer, request, query head) population mean/variance of the
- * raw scores, combined from the page moments in fp64; denom = sqrt(max(var, 1e-6)).
+ * raw scores, combined from the partial moments in fp64; denom = sqrt(max(var, 1e-6)).
+ * parts_per_page: 1 (kvc_score_paged_keys) or 4 (kvc_score_paged_keys_tc).
  * Replaces torch.var_mean(raw, dim=-1, correction=0) (methods/triattention/method.py:379-381,423)
  * and the denominator of normalize_head_scores (methods/triattention/scoring.py:123-128).
  * mean_out, var_out, denom_out: [L][R][kvh*G].
  */
 int kvc_head_stats(const float* partial, int num_layers, int num_requests, int total_pages,
-                   int heads, const int32_t* tokens, const int32_t* page_off, float* mean_out,
-                   float* var_out, float* denom_out, void* stream);
+                   int parts_per_page, int heads, const int32_t* tokens, const int32_t* page_off,
+                   float* mean_out, float* var_out, float* denom_out, void* stream);
 
 /*
  * Normalise (z = (raw - mean) / denom), max over the local query heads, then

@@ -207,9 +207,12 @@ def config0() -> Workload:
     return place_blocks(Workload("config0", geo, opts, [1000, 2500, 4096, 6000], seed=0, pool_pages=128))
 
 
-def config1(stride: int = 8, num_seqs: int = 32) -> Workload:
-    """Qwen2.5-14B-shaped ragged batch: 48 layers, 40/8 heads, D 128, B 4608."""
-    geo = Geometry(48, 8, 40, 128, 128, 1e6)
+def config1(stride: int = 8, num_seqs: int = 32, num_layers: int = 48) -> Workload:
+    """Qwen2.5-14B-shaped ragged batch: 48 layers, 40/8 heads, D 128, B 4608.
+
+    ``num_seqs``/``num_layers`` shrink it for profiling captures only.
+    """
+    geo = Geometry(num_layers, 8, 40, 128, 128, 1e6)
     opts = Options(kv_budget=4608, recompute_window=128, protected_prefix_window=128,
                    protected_recent_window=512, score_layer_stride=stride)
     return place_blocks(Workload("config1", geo, opts, _uniform_lengths(num_seqs, 4096, 32768, 1), seed=1))

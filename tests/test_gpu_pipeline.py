@@ -36,13 +36,17 @@ def _workload(name: str) -> W.Workload:
     return W.config0() if name == "config0" else golden_small_cases()[name]
 
 
-@pytest.mark.parametrize("name", ["config0", "partial", "global_max", "score_max"])
-def test_pipeline_matches_reference_golden(name, tmp_path):
+@pytest.mark.parametrize("name,scorer", [("config0", "auto"), ("partial", "auto"), ("global_max", "auto"),
+                                         ("score_max", "auto"), ("config0", "fma"), ("partial", "fma")])
+def test_pipeline_matches_reference_golden(name, scorer, tmp_path, monkeypatch):
+    monkeypatch.setenv("KVC_B200_SCORER", scorer)
     arrays, spec = golden()
     w = _workload(name)
     cpu = cpu_caches(w)
     gpu = to_gpu(cpu)
     m = bind(w, gpu, tmp_path)
+    if name != "score_max" and scorer == "auto":
+        assert m.use_tensor_scorer, "supported geometry must take the tensor-core scorer"
     reqs = W.b200_requests(w)
     idx = w.compressed()
     keep = m.select_many(reqs).cpu()
@@ -74,6 +78,20 @@ def test_pipeline_matches_reference_golden(name, tmp_path):
             for li, (kg, vg) in enumerate(gpu):
                 assert _sha(kg[dst.cuda()].cpu()) == spec[name]["dest_hashes"][f"r{i}/layer{li}/k"]
                 assert _sha(vg[dst.cuda()].cpu()) == spec[name]["dest_hashes"][f"r{i}/layer{li}/v"]
+
+
+def test_tensor_and_cuda_core_scorers_agree(tmp_path, monkeypatch):
+    w = W.config0()
+    gpu = to_gpu(cpu_caches(w))
+    out = {}
+    for scorer in ("tensor", "fma"):
+        monkeypatch.setenv("KVC_B200_SCORER", scorer)
+        m = bind(w, gpu, tmp_path)
+        m.select_many(W.b200_requests(w))
+        out[scorer] = [t.detach().clone().cpu() for t in m.last_stats]
+    for a, b in zip(out["tensor"][1:], out["fma"][1:]):  # mean, var, agg
+        finite = torch.isfinite(b)
+        assert_scores_close(a[finite], b[finite], tol=2e-4)
 
 
 def test_per_request_compress_equals_batched(tmp_path):

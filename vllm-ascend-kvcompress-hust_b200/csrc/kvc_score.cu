@@ -383,20 +383,21 @@ __device__ __forceinline__ Moments chan(Moments x, Moments y) {
 }
 
 __global__ void __launch_bounds__(256) head_stats_kernel(const float* __restrict__ partial, int L, int R,
-                                                         int total_pages, int heads,
+                                                         int total_pages, int parts, int heads,
                                                          const int32_t* __restrict__ tokens,
                                                          const int32_t* __restrict__ page_off,
                                                          float* mean_out, float* var_out, float* den_out) {
   const int l = blockIdx.x, r = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int p0 = page_off[r], p1 = page_off[r + 1], T = tokens[r];
-  const float2* part = reinterpret_cast<const float2*>(partial) + (int64_t)l * total_pages * heads;
+  const int span = kBlock / parts;  // tokens per partial
+  const float2* part = reinterpret_cast<const float2*>(partial) + (int64_t)l * total_pages * parts * heads;
   for (int hg = warp; hg < heads; hg += blockDim.x >> 5) {
     Moments m{0, 0, 0};
-    for (int p = p0 + lane; p < p1; p += 32) {
-      const int n = min(kBlock, T - (p - p0) * kBlock);
+    for (int q = p0 * parts + lane; q < p1 * parts; q += 32) {
+      const int n = min(span, T - (q - p0 * parts) * span);
       if (n <= 0) continue;
-      const float2 v = part[(int64_t)p * heads + hg];
+      const float2 v = part[(int64_t)q * heads + hg];
       m = chan(m, Moments{(double)n, (double)v.x / n, (double)v.y});
     }
 #pragma unroll
@@ -613,14 +614,15 @@ extern "C" int kvc_score_paged_keys(const void* const* k_layers, int L, int dtyp
   return dtype == KVC_BF16 ? dispatch_group<Bf16>(a, G, aggregation, st) : dispatch_group<Fp16>(a, G, aggregation, st);
 }
 
-extern "C" int kvc_head_stats(const float* partial, int L, int R, int total_pages, int heads,
+extern "C" int kvc_head_stats(const float* partial, int L, int R, int total_pages, int parts_per_page, int heads,
                               const int32_t* tokens, const int32_t* page_off, float* mean_out,
                               float* var_out, float* denom_out, void* stream) {
   KVC_CHECK_ARG(partial && tokens && page_off && mean_out && var_out && denom_out, KVC_ENULL);
   KVC_CHECK_ARG(L > 0 && R >= 0 && heads > 0 && total_pages >= 0, KVC_EINVAL);
+  KVC_CHECK_ARG(parts_per_page == 1 || parts_per_page == 4, KVC_EINVAL);
   if (R == 0) return KVC_OK;
-  head_stats_kernel<<<dim3(L, R), 256, 0, (cudaStream_t)stream>>>(partial, L, R, total_pages, heads, tokens,
-                                                                  page_off, mean_out, var_out, denom_out);
+  head_stats_kernel<<<dim3(L, R), 256, 0, (cudaStream_t)stream>>>(partial, L, R, total_pages, parts_per_page, heads,
+                                                                  tokens, page_off, mean_out, var_out, denom_out);
   return launch_status();
 }
 

@@ -1,0 +1,611 @@
+// Tensor-core trigonometric key scorer for sm_100a: TMA-staged pages, bf16 MMA.
+//
+// Per (scoring layer l, KV head h, request r) the raw score of every cached key
+// is a small matrix product: for the 128 tokens of a page
+//     Y[t, g] = sum_k X[t, k] * W[k, g]
+//     X = [ kr | ki | m_hi | m_lo | k_pass ]      (m = sqrt(kr^2 + ki^2))
+//     W = [ a  | b  |  e   |  e   | q_pass ]      (a, b, e folded with the phases)
+// Keys are exact in bf16 (they are bf16 in the cache); the fp32 coefficients
+// are split into hi + lo bf16 parts held in the two 8-column halves of a
+// 16-column B operand (Y[:, g] = C[:, g] + C[:, 8 + g]), and m into
+// m_hi + m_lo; the dropped m_lo * e_lo term is ~2^-18 relative.  The MMA
+// accumulates in fp32.  This keeps fp32-level agreement with the reference's
+// fp32 scorer at a fraction of the CUDA-core instruction count.
+//
+// Data path: a producer warp streams each (page, head) K tile (128 tokens x
+// head_dim) from the paged cache with cp.async.bulk.tensor (4-D tensor map
+// over [blocks][128][kv_heads][head_dim], 64-element boxes, 128-byte swizzle)
+// into a ring of shared-memory stages guarded by mbarriers; four consumer
+// warps each own 32 tokens (two m16 tiles), load A fragments with ldmatrix
+// (conflict-free on the swizzled layout), compute m in registers from the kr/ki
+// fragments, and issue mma.sync.m16n8k16.  Every wait is bounded by a
+// global-timer deadline; on expiry the kernel raises KVC_DEV_TIMEOUT and exits.
+//
+// The B-operand fragments of W are produced once per (request, layer, head) by
+// prepare_frag_kernel directly in the per-lane register layout, so a consumer
+// loads them with 16-byte coalesced loads when its unit's (r, l, h) changes.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "kvc_common.cuh"
+
+namespace kvc {
+
+constexpr int kTcConsumers = 4;
+constexpr int kTcThreads = (kTcConsumers + 1) * 32;
+constexpr int kMaxTcLayers = 64;
+constexpr int kBoxElems = 64;                   // 128-byte swizzle span of 16-bit elements
+constexpr int kBoxBytes = kBoxElems * 2 * kBlock;  // one box: 128 tokens x 64 elements = 16 KB
+constexpr uint64_t kWaitNs = 2000000000ull;     // bounded mbarrier waits (2 s)
+
+__host__ __device__ constexpr int frag_steps(int F, int P) { return 4 * (F / 16) + P / 16; }
+
+// ---------------------------------------------------------------------------
+// B-operand fragments of W (prepared once per (request, layer, head))
+// ---------------------------------------------------------------------------
+
+struct FragArgs {
+  const float* omega;     // [L][F]
+  const float* offsets;   // [n_off]
+  const int64_t* round_start;
+  const float* q_real;    // [L][kvh][G][F]
+  const float* q_imag;
+  const float* scale;
+  const float* extra;
+  const float* q_pass;    // [L][kvh][G][P] or null
+  uint32_t* frag;         // [R][L][kvh][S][32 lanes][4 words]
+  int n_off, R, L, kvh, G, F, P, half_fp16;
+};
+
+__device__ __forceinline__ uint16_t to_half_bits(float v, int fp16) {
+  if (fp16) {
+    __half h = __float2half_rn(v);
+    return *reinterpret_cast<uint16_t*>(&h);
+  }
+  __nv_bfloat16 b = __float2bfloat16_rn(v);
+  return *reinterpret_cast<uint16_t*>(&b);
+}
+
+__device__ __forceinline__ float from_half_bits(uint16_t v, int fp16) {
+  return fp16 ? unpack1(v, Fp16{}) : unpack1(v, Bf16{});
+}
+
+__global__ void __launch_bounds__(256) prepare_frag_kernel(const __grid_constant__ FragArgs a) {
+  extern __shared__ float sm[];
+  float* cm = sm;          // [F] mean cos
+  float* sn = sm + a.F;    // [F] mean sin
+  const int l = blockIdx.x, r = blockIdx.y;
+  const float rs = (float)a.round_start[r];
+  for (int f = threadIdx.x; f < a.F; f += blockDim.x) {
+    const float w = a.omega[l * a.F + f];
+    float cs = 0.f, ss = 0.f;
+    for (int o = 0; o < a.n_off; ++o) {
+      const float ph = __fmul_rn(__fadd_rn(a.offsets[o], rs), w);
+      float s, c;
+      sincosf(ph, &s, &c);
+      cs += c;
+      ss += s;
+    }
+    const float inv = 1.0f / (float)a.n_off;
+    cm[f] = cs * inv;
+    sn[f] = ss * inv;
+  }
+  __syncthreads();
+  const int S = frag_steps(a.F, a.P);
+  const int kf = a.F / 16;
+  const int64_t total = (int64_t)a.kvh * S * 32;
+  for (int64_t i = threadIdx.x; i < total; i += blockDim.x) {
+    const int lane = i % 32;
+    const int s = (i / 32) % S;
+    const int h = i / (32 * S);
+    uint32_t words[4];
+    for (int t = 0; t < 2; ++t) {          // n-tile: 0 = hi columns, 1 = lo columns
+      const int g = lane / 4;              // column within the n-tile = query head
+      for (int q = 0; q < 2; ++q) {        // register: k rows 0..7 / 8..15 of the step
+        uint32_t word = 0;
+        for (int e = 0; e < 2; ++e) {
+          const int k = 2 * (lane % 4) + 8 * q + e;  // row within the 16-row step
+          float v = 0.f;
+          bool lo_zero = false;
+          if (g < a.G) {
+            const int part = s < kf ? 0 : s < 2 * kf ? 1 : s < 3 * kf ? 2 : s < 4 * kf ? 3 : 4;
+            if (part < 4) {
+              const int f = (s - part * kf) * 16 + k;
+              const int64_t src = ((int64_t)(l * a.kvh + h) * a.G + g) * a.F + f;
+              const float qr = a.q_real[src], qi = a.q_imag[src], sc = a.scale[src];
+              if (part == 0) v = sc * (qr * cm[f] - qi * sn[f]);
+              else if (part == 1) v = sc * (qi * cm[f] + qr * sn[f]);
+              else v = a.extra[src] * sc;
+              lo_zero = part == 3;  // m_lo rows pair with e_hi only
+            } else {
+              const int p = (s - 4 * kf) * 16 + k;
+              v = a.q_pass[((int64_t)(l * a.kvh + h) * a.G + g) * a.P + p];
+            }
+          }
+          const uint16_t hi = to_half_bits(v, a.half_fp16);
+          uint16_t bits;
+          if (t == 0) bits = hi;
+          else bits = lo_zero ? 0 : to_half_bits(v - from_half_bits(hi, a.half_fp16), a.half_fp16);
+          word |= (uint32_t)bits << (16 * e);
+        }
+        words[2 * t + q] = word;
+      }
+    }
+    uint4* dst = reinterpret_cast<uint4*>(a.frag) +
+                 (((int64_t)(r * a.L + l) * a.kvh + h) * S + s) * 32 + lane;
+    *dst = make_uint4(words[0], words[1], words[2], words[3]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// PTX helpers (mbarrier, TMA, ldmatrix, mma)
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Wait until the phase with the given parity has completed, at most kWaitNs.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t* flag) {
+  uint64_t start = 0;
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (it == 0) start = global_ns();
+    else if ((it & 63) == 0 && global_ns() - start > kWaitNs) {
+      raise_flag(flag, KVC_DEV_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* map, int c0, int c1, int c2, int c3,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
+      ::"r"(dst), "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+template <class E>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
+
+template <>
+__device__ __forceinline__ void mma16816<Bf16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <>
+__device__ __forceinline__ void mma16816<Fp16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ float sqrt_approx(float x) {
+  float y;
+  asm("sqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, Bf16) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, Fp16) {
+  uint32_t d;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+// m = |(kr, ki)| for the 8 elements of an A fragment, split into hi + lo halves.
+template <class E>
+__device__ __forceinline__ void modulus_split(const uint32_t (&kr)[4], const uint32_t (&ki)[4], uint32_t (&hi)[4],
+                                              uint32_t (&lo)[4]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 r = unpack2(kr[i], E{});
+    const float2 m = unpack2(ki[i], E{});
+    const float m0 = sqrt_approx(r.x * r.x + m.x * m.x);
+    const float m1 = sqrt_approx(r.y * r.y + m.y * m.y);
+    hi[i] = pack2(m0, m1, E{});
+    const float2 h = unpack2(hi[i], E{});
+    lo[i] = pack2(m0 - h.x, m1 - h.y, E{});
+  }
+}
+
+// ---------------------------------------------------------------------------
+// the scorer
+// ---------------------------------------------------------------------------
+
+struct TcArgs {
+  CUtensorMap maps[kMaxTcLayers];
+  const int64_t* src_blocks;
+  const int64_t* src_block_off;
+  const int32_t* tokens;
+  const int32_t* page_off;
+  const uint4* frag;
+  float* raw;
+  float* partial;
+  int32_t* error_flag;
+  int64_t tok_total;
+  int64_t num_blocks;
+  int64_t units;        // layers_here * kvh * total_pages
+  int layer0;           // global index of maps[0]
+  int L_total;          // scoring layers (raw / partial / frag indexing)
+  int kvh, G, R, total_pages;
+};
+
+template <int F, int P>
+struct TcGeom {
+  static constexpr int D = 2 * F + P;
+  static constexpr int S = frag_steps(F, P);
+  static constexpr int kBoxes = D / kBoxElems;
+  static constexpr int kStageBytes = kBoxes * kBoxBytes;
+  static constexpr int kStages = D <= 128 ? 3 : 2;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 + 64;
+  static constexpr int kMinBlocks = D <= 128 ? 2 : 1;
+};
+
+// Shared-memory byte address of 16-element column group `col16` (dims col16*16 ..)
+// of the 16-row tile starting at `row0`, for this lane's ldmatrix.x4 row.
+__device__ __forceinline__ uint32_t frag_addr(uint32_t stage, int row0, int dim0, int lane) {
+  const int row = row0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+  const int dim = dim0 + (lane >> 4) * 8;
+  const int box = dim / kBoxElems;
+  const int chunk = (dim % kBoxElems) / 8;
+  return stage + box * kBoxBytes + row * 128 + ((chunk ^ (row & 7)) << 4);
+}
+
+template <int F, int P, class E>
+__global__ void __launch_bounds__(kTcThreads, TcGeom<F, P>::kMinBlocks) score_tc_kernel(const __grid_constant__ TcArgs a) {
+  using Gm = TcGeom<F, P>;
+  constexpr int S = Gm::S;
+  constexpr int KF = F / 16;
+  constexpr int KP = P / 16;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + Gm::kStages * Gm::kStageBytes);
+  const uint32_t stage0 = smem_u32(base);
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + Gm::kStages);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Gm::kStages; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, kTcConsumers);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  const int64_t per = (a.units + gridDim.x - 1) / gridDim.x;
+  const int64_t u0 = (int64_t)blockIdx.x * per;
+  const int64_t u1 = min64(a.units, u0 + per);
+  const int heads = a.kvh * a.G;
+
+  if (warp == kTcConsumers) {
+    // ---------------- producer: one elected lane issues the TMA tiles ----------
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int64_t u = u0; u < u1; ++u) {
+        const int p = (int)(u % a.total_pages);
+        const int h = (int)((u / a.total_pages) % a.kvh);
+        const int l = (int)(u / ((int64_t)a.total_pages * a.kvh));
+        const int r = request_of_page(a.page_off, a.R, p);
+        const int pl = p - __ldg(a.page_off + r);
+        const int64_t blk = __ldg(a.src_blocks + __ldg(a.src_block_off + r) + pl);
+        if (blk < 0 || blk >= a.num_blocks) continue;  // consumers skip the same unit
+        const int s = it % Gm::kStages;
+        const uint32_t ph = (it / Gm::kStages) & 1;
+        if (!mbar_wait(empty0 + 8 * s, ph ^ 1, a.error_flag)) break;
+        mbar_expect_tx(full0 + 8 * s, Gm::kStageBytes);
+#pragma unroll
+        for (int b = 0; b < Gm::kBoxes; ++b)
+          tma_load_4d(stage0 + s * Gm::kStageBytes + b * kBoxBytes, &a.maps[l], b * kBoxElems, h, 0, (int)blk,
+                      full0 + 8 * s);
+        ++it;
+      }
+      // drain: every issued tile must have landed before the CTA may exit
+      for (uint32_t k = 0; k < Gm::kStages && k < it; ++k) {
+        const uint32_t j = it - 1 - k;
+        mbar_wait(full0 + 8 * (j % Gm::kStages), (j / Gm::kStages) & 1, a.error_flag);
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers: 4 warps x 32 tokens of each 128-token tile ----
+  uint4 w[S];
+  int cur_key = -1;
+  uint32_t it = 0;
+  for (int64_t u = u0; u < u1; ++u) {
+    const int p = (int)(u % a.total_pages);
+    const int h = (int)((u / a.total_pages) % a.kvh);
+    const int l = (int)(u / ((int64_t)a.total_pages * a.kvh));
+    const int r = request_of_page(a.page_off, a.R, p);
+    const int pl = p - __ldg(a.page_off + r);
+    const int valid = min(kBlock, __ldg(a.tokens + r) - pl * kBlock);
+    const int64_t blk = __ldg(a.src_blocks + __ldg(a.src_block_off + r) + pl);
+    if (blk < 0 || blk >= a.num_blocks) {
+      if (warp == 0 && lane == 0) raise_flag(a.error_flag, KVC_DEV_BLOCK_RANGE);
+      continue;
+    }
+    const int lg = a.layer0 + l;
+    const int key = (r * a.L_total + lg) * a.kvh + h;
+    if (key != cur_key) {
+      const uint4* src = a.frag + (int64_t)key * S * 32 + lane;
+#pragma unroll
+      for (int s = 0; s < S; ++s) w[s] = __ldg(src + s * 32);
+      cur_key = key;
+    }
+    const int s = it % Gm::kStages;
+    const uint32_t ph = (it / Gm::kStages) & 1;
+    ++it;
+    if (!mbar_wait(full0 + 8 * s, ph, a.error_flag)) return;
+    const uint32_t stage = stage0 + s * Gm::kStageBytes;
+
+    float y[2][4];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      const int row0 = warp * 32 + mt * 16;
+      float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < KF; ++j) {
+        uint32_t kr[4], ki[4], mh[4], ml[4];
+        ldsm_x4(frag_addr(stage, row0, 16 * j, lane), kr);
+        ldsm_x4(frag_addr(stage, row0, F + 16 * j, lane), ki);
+        mma16816<E>(c0, kr, w[j].x, w[j].y);
+        mma16816<E>(c1, kr, w[j].z, w[j].w);
+        mma16816<E>(c0, ki, w[KF + j].x, w[KF + j].y);
+        mma16816<E>(c1, ki, w[KF + j].z, w[KF + j].w);
+        modulus_split<E>(kr, ki, mh, ml);
+        mma16816<E>(c0, mh, w[2 * KF + j].x, w[2 * KF + j].y);
+        mma16816<E>(c1, mh, w[2 * KF + j].z, w[2 * KF + j].w);
+        mma16816<E>(c0, ml, w[3 * KF + j].x, w[3 * KF + j].y);
+      }
+#pragma unroll
+      for (int j = 0; j < KP; ++j) {
+        uint32_t kp[4];
+        ldsm_x4(frag_addr(stage, row0, 2 * F + 16 * j, lane), kp);
+        mma16816<E>(c0, kp, w[4 * KF + j].x, w[4 * KF + j].y);
+        mma16816<E>(c1, kp, w[4 * KF + j].z, w[4 * KF + j].w);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) y[mt][i] = c0[i] + c1[i];
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty0 + 8 * s);
+
+    // ---- epilogue: raw scores and the quarter-page moments of each query head
+    // lane holds heads g = 2*(lane%4) + {0,1} for tokens warp*32 + {0,8,16,24} + lane/4
+    const int nq = max(0, min(32, valid - warp * 32));
+#pragma unroll
+    for (int gi = 0; gi < 2; ++gi) {
+      const int g = 2 * (lane & 3) + gi;
+      float vals[4];
+      bool ok[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int mt = i >> 1, half = i & 1;
+        const int t = warp * 32 + mt * 16 + half * 8 + (lane >> 2);
+        vals[i] = y[mt][half * 2 + gi];
+        ok[i] = t < valid && g < a.G;
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sum += ok[i] ? vals[i] : 0.f;
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      const float mu = nq > 0 ? sum / (float)nq : 0.f;
+      float m2 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float d = vals[i] - mu;
+        m2 += ok[i] ? d * d : 0.f;
+      }
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) m2 += __shfl_xor_sync(0xffffffffu, m2, o);
+      if (g < a.G) {
+        float* row = a.raw + ((int64_t)lg * heads + h * a.G + g) * a.tok_total + (int64_t)p * kBlock;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int t = warp * 32 + (i >> 1) * 16 + (i & 1) * 8 + (lane >> 2);
+          if (ok[i]) row[t] = vals[i];
+        }
+        if (lane < 4) {
+          float2* out = reinterpret_cast<float2*>(a.partial) +
+                        (((int64_t)lg * a.total_pages + p) * 4 + warp) * heads + h * a.G + g;
+          *out = make_float2(sum, m2);
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+template <int F, int P, class E>
+int launch_tc(const TcArgs& a, cudaStream_t st) {
+  using Gm = TcGeom<F, P>;
+  if (a.units == 0) return KVC_OK;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(score_tc_kernel<F, P, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, Gm::kSmem) !=
+        cudaSuccess)
+      return KVC_ECUDA;
+    configured = true;
+  }
+  const int64_t cap = (int64_t)sm_count() * Gm::kMinBlocks;
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cap, a.units));
+  score_tc_kernel<F, P, E><<<grid, kTcThreads, Gm::kSmem, st>>>(a);
+  return launch_status();
+}
+
+template <class E>
+int dispatch_tc(const TcArgs& a, int F, int P, cudaStream_t st) {
+  if (F == 64 && P == 0) return launch_tc<64, 0, E>(a, st);
+  if (F == 32 && P == 0) return launch_tc<32, 0, E>(a, st);
+  if (F == 32 && P == 192) return launch_tc<32, 192, E>(a, st);
+  if (F == 32 && P == 64) return launch_tc<32, 64, E>(a, st);
+  if (F == 64 && P == 128) return launch_tc<64, 128, E>(a, st);
+  if (F == 128 && P == 0) return launch_tc<128, 0, E>(a, st);
+  return KVC_EUNSUPPORTED;
+}
+
+bool tc_geometry_supported(int G, int D, int rot) {
+  const int F = rot / 2, P = D - rot;
+  if (G < 1 || G > 8 || rot % 2) return false;
+  return (F == 64 && P == 0) || (F == 32 && P == 0) || (F == 32 && P == 192) || (F == 32 && P == 64) ||
+         (F == 64 && P == 128) || (F == 128 && P == 0);
+}
+
+}  // namespace kvc
+
+using namespace kvc;
+
+extern "C" int kvc_tc_supported(int group, int head_dim, int rotary_dim) {
+  return tc_geometry_supported(group, head_dim, rotary_dim) ? 1 : 0;
+}
+
+extern "C" int64_t kvc_fragment_words(int num_freq, int pass_dim) {
+  if (num_freq <= 0 || num_freq % 16 || pass_dim < 0 || pass_dim % 16) return 0;
+  return (int64_t)frag_steps(num_freq, pass_dim) * 32 * 4;
+}
+
+extern "C" int kvc_encode_key_maps(const void* const* k_layers, int L, int dtype, int64_t block_stride,
+                                   int64_t num_blocks, int kvh, int D, void* maps_out) {
+  KVC_CHECK_ARG(k_layers && maps_out, KVC_ENULL);
+  KVC_CHECK_ARG(L > 0 && kvh > 0 && D > 0 && num_blocks > 0 && (dtype == KVC_BF16 || dtype == KVC_FP16),
+                KVC_EINVAL);
+  KVC_CHECK_ARG(D % kBoxElems == 0, KVC_EUNSUPPORTED);
+  KVC_CHECK_ARG(block_stride >= (int64_t)kBlock * kvh * D && (block_stride * 2) % 16 == 0, KVC_EALIGN);
+  PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+  if (!fn) return KVC_ECUDA;
+  unsigned char* out = reinterpret_cast<unsigned char*>(maps_out);  // caller's buffer: any alignment
+  for (int l = 0; l < L; ++l) {
+    KVC_CHECK_ARG(k_layers[l] != nullptr, KVC_ENULL);
+    KVC_CHECK_ARG(aligned(k_layers[l], 16), KVC_EALIGN);
+    const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)kvh, (cuuint64_t)kBlock, (cuuint64_t)num_blocks};
+    const cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)kvh * D * 2, (cuuint64_t)block_stride * 2};
+    const cuuint32_t box[4] = {kBoxElems, 1, kBlock, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUtensorMap tmp;
+    const CUresult rc = fn(&tmp, dtype == KVC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                           4, const_cast<void*>(k_layers[l]), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (rc != CUDA_SUCCESS) return KVC_EINVAL;
+    memcpy(out + (size_t)l * sizeof(CUtensorMap), &tmp, sizeof(CUtensorMap));
+  }
+  return KVC_OK;
+}
+
+extern "C" int kvc_prepare_score_fragments(const float* omega, const float* offsets, int n_off,
+                                           const int64_t* round_start, int R, int L, int kvh, int G, int F, int P,
+                                           const float* q_real, const float* q_imag, const float* scale,
+                                           const float* extra, const float* q_pass, int dtype, uint32_t* frag_out,
+                                           void* stream) {
+  KVC_CHECK_ARG(omega && offsets && round_start && q_real && q_imag && scale && extra && frag_out, KVC_ENULL);
+  KVC_CHECK_ARG(n_off > 0 && n_off <= 64 && R >= 0 && L > 0 && kvh > 0 && G > 0 && G <= 8, KVC_EINVAL);
+  KVC_CHECK_ARG(F > 0 && F % 16 == 0 && P >= 0 && P % 16 == 0, KVC_EUNSUPPORTED);
+  KVC_CHECK_ARG(P == 0 || q_pass != nullptr, KVC_ENULL);
+  KVC_CHECK_ARG(dtype == KVC_BF16 || dtype == KVC_FP16, KVC_EINVAL);
+  KVC_CHECK_ARG(aligned(frag_out, 16), KVC_EALIGN);
+  if (R == 0) return KVC_OK;
+  FragArgs a{omega, offsets, round_start, q_real, q_imag, scale, extra, q_pass, frag_out,
+             n_off, R, L, kvh, G, F, P, dtype == KVC_FP16 ? 1 : 0};
+  prepare_frag_kernel<<<dim3(L, R), 256, 2 * F * sizeof(float), (cudaStream_t)stream>>>(a);
+  return launch_status();
+}
+
+extern "C" int kvc_score_paged_keys_tc(const void* key_maps, int L, int dtype, int64_t num_blocks, int kvh, int G,
+                                       int D, int rot, const int64_t* src_blocks, const int64_t* src_block_off,
+                                       const int32_t* tokens, const int32_t* page_off, int R, int total_pages,
+                                       const uint32_t* frag, float* raw_out, float* partial_out,
+                                       int32_t* error_flag, void* stream) {
+  KVC_CHECK_ARG(key_maps && src_blocks && src_block_off && tokens && page_off && frag && raw_out && partial_out,
+                KVC_ENULL);
+  KVC_CHECK_ARG(L > 0 && kvh > 0 && R >= 0 && total_pages >= 0 && num_blocks > 0, KVC_EINVAL);
+  KVC_CHECK_ARG(dtype == KVC_BF16 || dtype == KVC_FP16, KVC_EINVAL);
+  KVC_CHECK_ARG(tc_geometry_supported(G, D, rot), KVC_EUNSUPPORTED);
+  KVC_CHECK_ARG(aligned(frag, 16) && aligned(partial_out, 8), KVC_EALIGN);
+  if (R == 0 || total_pages == 0) return KVC_OK;
+  const unsigned char* maps = reinterpret_cast<const unsigned char*>(key_maps);
+  cudaStream_t st = (cudaStream_t)stream;
+  for (int l0 = 0; l0 < L; l0 += kMaxTcLayers) {
+    TcArgs a{};
+    const int nl = std::min(kMaxTcLayers, L - l0);
+    memcpy(a.maps, maps + (size_t)l0 * sizeof(CUtensorMap), sizeof(CUtensorMap) * nl);
+    a.src_blocks = src_blocks;
+    a.src_block_off = src_block_off;
+    a.tokens = tokens;
+    a.page_off = page_off;
+    a.frag = reinterpret_cast<const uint4*>(frag);
+    a.raw = raw_out;
+    a.partial = partial_out;
+    a.error_flag = error_flag;
+    a.tok_total = (int64_t)total_pages * kBlock;
+    a.num_blocks = num_blocks;
+    a.units = (int64_t)nl * kvh * total_pages;
+    a.layer0 = l0;
+    a.L_total = L;
+    a.kvh = kvh;
+    a.G = G;
+    a.R = R;
+    a.total_pages = total_pages;
+    const int F = rot / 2, P = D - rot;
+    const int rc = dtype == KVC_BF16 ? dispatch_tc<Bf16>(a, F, P, st) : dispatch_tc<Fp16>(a, F, P, st);
+    if (rc != KVC_OK) return rc;
+  }
+  return KVC_OK;
+}

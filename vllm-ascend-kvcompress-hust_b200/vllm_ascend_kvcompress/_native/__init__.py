@@ -17,7 +17,8 @@ LIB_NAME = "libkvc_b200.so"
 
 KVC_OK = 0
 STATUS = {0: "ok", -22: "EINVAL", -14: "ENULL", -71: "EALIGN", -95: "EUNSUPPORTED", -5: "ECUDA"}
-DEV_BLOCK_RANGE, DEV_TOKEN_RANGE, DEV_BUDGET = 1, 2, 4
+DEV_BLOCK_RANGE, DEV_TOKEN_RANGE, DEV_BUDGET, DEV_TIMEOUT = 1, 2, 4, 8
+TENSOR_MAP_BYTES = 128
 BF16, FP16 = 0, 1
 AGG_MEAN, AGG_MAX = 0, 1
 POLICY_GLOBAL, POLICY_V3 = 0, 1
@@ -32,7 +33,15 @@ _SIGNATURES = {
     "kvc_score_paged_keys": (
         c_int, [_P, c_int, c_int, c_int64, c_int64, c_int, c_int, c_int, c_int, _P, _P, _P, _P, c_int, c_int,
                 _P, c_int, c_int, _P, _P, _P, _P, _P]),
-    "kvc_head_stats": (c_int, [_P, c_int, c_int, c_int, c_int, _P, _P, _P, _P, _P, _P]),
+    "kvc_head_stats": (c_int, [_P, c_int, c_int, c_int, c_int, c_int, _P, _P, _P, _P, _P, _P]),
+    "kvc_tc_supported": (c_int, [c_int, c_int, c_int]),
+    "kvc_encode_key_maps": (c_int, [_P, c_int, c_int, c_int64, c_int64, c_int, c_int, _P]),
+    "kvc_fragment_words": (c_int64, [c_int, c_int]),
+    "kvc_prepare_score_fragments": (
+        c_int, [_P, _P, c_int, _P, c_int, c_int, c_int, c_int, c_int, c_int, _P, _P, _P, _P, _P, c_int, _P, _P]),
+    "kvc_score_paged_keys_tc": (
+        c_int, [_P, c_int, c_int, c_int64, c_int, c_int, c_int, c_int, _P, _P, _P, _P, c_int, c_int, _P, _P, _P,
+                _P, _P]),
     "kvc_normalize_aggregate": (c_int, [_P, c_int, c_int, c_int, _P, _P, _P, _P, c_int, c_int, _P, _P, _P]),
     "kvc_aggregate_rows": (c_int, [_P, c_int, c_int, _P, _P, c_int, c_int, _P, _P]),
     "kvc_select_keep": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int, _P, _P, _P]),

@@ -13,8 +13,8 @@ of selection.py / cache.py / method.py):
 this module                    reference
 =============================  =====================================================
 prepare_score_coefficients     prepare_mean_phase_coefficients (kernels.py:85-122),
-                               phase formation of score_post_rope_keys (scoring.py:77-83)
-score_paged_keys               score_paged_keys_mean_precomputed (kernels.py:247-317)
+prepare_score_fragments        phase formation of score_post_rope_keys (scoring.py:77-83)
+score_paged_keys(_tc)          score_paged_keys_mean_precomputed (kernels.py:247-317)
 head_stats                     torch.var_mean(..., correction=0) (method.py:379,423)
 normalize_aggregate            aggregate_normalized_scores (kernels.py:407-437),
                                _aggregate_torch (method.py:477-503), method.py:463-467
@@ -118,10 +118,49 @@ def score_paged_keys(k_ptrs, dtype: torch.dtype, block_stride: int, num_blocks: 
         _p(error_flag), _stream()), "kvc_score_paged_keys")
 
 
-def head_stats(partial, num_layers: int, heads: int, plan: BatchPlan, mean_out, var_out, den_out) -> None:
+def tc_supported(group: int, head_dim: int, rotary_dim: int) -> bool:
+    return bool(N.lib().kvc_tc_supported(group, head_dim, rotary_dim))
+
+
+def encode_key_maps(k_ptrs, dtype: torch.dtype, block_stride: int, num_blocks: int, kvh: int, head_dim: int):
+    """Host buffer of one 128-byte TMA descriptor per K cache (built once per binding)."""
+    import ctypes
+
+    buf = ctypes.create_string_buffer(len(k_ptrs) * N.TENSOR_MAP_BYTES)
+    N.check(N.lib().kvc_encode_key_maps(k_ptrs, len(k_ptrs), _dtype_code(dtype), block_stride, num_blocks, kvh,
+                                        head_dim, buf), "kvc_encode_key_maps")
+    return buf
+
+
+def fragment_words(num_freq: int, pass_dim: int) -> int:
+    return int(N.lib().kvc_fragment_words(num_freq, pass_dim))
+
+
+def prepare_score_fragments(omega, offsets, plan: BatchPlan, q_real, q_imag, scale, extra, q_pass,
+                            dtype: torch.dtype, frag_out) -> None:
+    L, kvh, G, F = q_real.shape
+    P = 0 if q_pass is None else q_pass.shape[-1]
+    N.check(N.lib().kvc_prepare_score_fragments(
+        _p(omega), _p(offsets), offsets.numel(), _p(plan.round_start), plan.num_requests, L, kvh, G, F, P,
+        _p(q_real), _p(q_imag), _p(scale), _p(extra), _p(q_pass), _dtype_code(dtype), _p(frag_out), _stream()),
+        "kvc_prepare_score_fragments")
+
+
+def score_paged_keys_tc(key_maps, num_layers: int, dtype: torch.dtype, num_blocks: int, kvh: int, group: int,
+                        head_dim: int, rotary_dim: int, plan: BatchPlan, frag, raw_out, partial_out,
+                        error_flag) -> None:
+    N.check(N.lib().kvc_score_paged_keys_tc(
+        key_maps, num_layers, _dtype_code(dtype), num_blocks, kvh, group, head_dim, rotary_dim,
+        _p(plan.src_blocks), _p(plan.src_off), _p(plan.tokens), _p(plan.page_off), plan.num_requests,
+        plan.total_pages, _p(frag), _p(raw_out), _p(partial_out), _p(error_flag), _stream()),
+        "kvc_score_paged_keys_tc")
+
+
+def head_stats(partial, num_layers: int, heads: int, plan: BatchPlan, mean_out, var_out, den_out,
+               parts_per_page: int = 1) -> None:
     N.check(N.lib().kvc_head_stats(
-        _p(partial), num_layers, plan.num_requests, plan.total_pages, heads, _p(plan.tokens), _p(plan.page_off),
-        _p(mean_out), _p(var_out), _p(den_out), _stream()), "kvc_head_stats")
+        _p(partial), num_layers, plan.num_requests, plan.total_pages, parts_per_page, heads, _p(plan.tokens),
+        _p(plan.page_off), _p(mean_out), _p(var_out), _p(den_out), _stream()), "kvc_head_stats")
 
 
 def normalize_aggregate(raw, num_layers: int, heads: int, plan: BatchPlan, mean, den, layer_aggregation: int,

@@ -45,6 +45,7 @@ from .stats import CalibrationStats, DeviceLayerCalibrationStats
 
 METHOD_NAME = "triattention"
 _STRICT_ENV = "KVC_B200_STRICT"
+_SCORER_ENV = "KVC_B200_SCORER"
 
 
 def _queries_per_kv_head(shape: ModelShape) -> int:
@@ -103,6 +104,8 @@ class TriAttentionMethod(KVCompressionMethod):
         self.staged_block_rows: torch.Tensor | None = None
         self.staged_offsets: torch.Tensor | None = None
         self.profiler = None  # optional object with .mark(name) (bench timing hooks)
+        # "auto": tensor-core scorer where the geometry allows, else the CUDA-core one
+        self.scorer = "auto"
         self._ws: _Workspaces | None = None
         self._err_host: torch.Tensor | None = None
         self._err_event: torch.cuda.Event | None = None
@@ -305,6 +308,20 @@ class TriAttentionMethod(KVCompressionMethod):
         self.score_aggregation_code = N.AGG_MEAN if self.config.score_aggregation == "mean" else N.AGG_MAX
         self.layer_aggregation_code = N.AGG_MEAN if self.config.layer_aggregation == "mean" else N.AGG_MAX
         self.coef_block = K.coef_floats(self.num_freq, self.group, self.offsets.numel(), self.score_aggregation_code)
+        choice = os.environ.get(_SCORER_ENV, self.scorer)
+        if choice not in ("auto", "tensor", "fma"):
+            raise ValueError(f"{_SCORER_ENV} must be auto, tensor or fma")
+        tc_ok = (self.config.score_aggregation == "mean"
+                 and K.tc_supported(self.group, self.head_dim, self.rotary_dim)
+                 and (self.block_stride * 2) % 16 == 0)
+        if choice == "tensor" and not tc_ok:
+            raise RuntimeError("the tensor-core scorer does not support this geometry/aggregation")
+        self.use_tensor_scorer = tc_ok and choice != "fma"
+        if self.use_tensor_scorer:
+            self._key_maps = K.encode_key_maps(self._k_score, self.kv_dtype, self.block_stride, self.num_blocks,
+                                               self.local_kv_heads, self.head_dim)
+            self.scoring_q_pass = stack(lambda c: c.stats.q_pass_mean) if self.pass_dim else None
+            self.frag_block = K.fragment_words(self.num_freq, self.pass_dim)
 
     # ---- per-step pipeline ----------------------------------------------------
 
@@ -361,24 +378,35 @@ class TriAttentionMethod(KVCompressionMethod):
         L = self.scoring_layer_count
         heads = self.local_kv_heads * self.group
         R, tok = plan.num_requests, plan.tok_total
-        coef = ws.get("coef", R * L * self.local_kv_heads * self.coef_block, torch.float32)
+        parts = 4 if self.use_tensor_scorer else 1
         raw = ws.get("raw", L * heads * tok, torch.float32)
-        partial = ws.get("partial", L * plan.total_pages * heads * 2, torch.float32)
+        partial = ws.get("partial", L * plan.total_pages * parts * heads * 2, torch.float32)
         mean = ws.get("mean", L * R * heads, torch.float32)
         var = ws.get("var", L * R * heads, torch.float32)
         den = ws.get("den", L * R * heads, torch.float32)
         agg = ws.get("agg", tok, torch.float32)
         keep = ws.get("keep", R * cfg.kv_budget, torch.int64)
         self._mark("prepare")
-        K.prepare_score_coefficients(self.scoring_omega, self.offsets, plan, self.scoring_q_real,
-                                     self.scoring_q_imag, self.scoring_scale, self.scoring_extra,
-                                     self.score_aggregation_code, coef)
-        self._mark("score")
-        K.score_paged_keys(self._k_score, self.kv_dtype, self.block_stride, self.num_blocks, self.local_kv_heads,
-                           self.group, self.head_dim, self.rotary_dim, plan, coef, self.offsets.numel(),
-                           self.score_aggregation_code, self.scoring_q_pass_t, raw, partial, self._err)
+        if self.use_tensor_scorer:
+            frag = ws.get("frag", R * L * self.local_kv_heads * self.frag_block, torch.int32)
+            K.prepare_score_fragments(self.scoring_omega, self.offsets, plan, self.scoring_q_real,
+                                      self.scoring_q_imag, self.scoring_scale, self.scoring_extra,
+                                      self.scoring_q_pass, self.kv_dtype, frag)
+            self._mark("score")
+            K.score_paged_keys_tc(self._key_maps, L, self.kv_dtype, self.num_blocks, self.local_kv_heads,
+                                  self.group, self.head_dim, self.rotary_dim, plan, frag, raw, partial, self._err)
+        else:
+            coef = ws.get("coef", R * L * self.local_kv_heads * self.coef_block, torch.float32)
+            K.prepare_score_coefficients(self.scoring_omega, self.offsets, plan, self.scoring_q_real,
+                                         self.scoring_q_imag, self.scoring_scale, self.scoring_extra,
+                                         self.score_aggregation_code, coef)
+            self._mark("score")
+            K.score_paged_keys(self._k_score, self.kv_dtype, self.block_stride, self.num_blocks,
+                               self.local_kv_heads, self.group, self.head_dim, self.rotary_dim, plan, coef,
+                               self.offsets.numel(), self.score_aggregation_code, self.scoring_q_pass_t, raw,
+                               partial, self._err)
         self._mark("head_stats")
-        K.head_stats(partial, L, heads, plan, mean, var, den)
+        K.head_stats(partial, L, heads, plan, mean, var, den, parts)
         self._mark("normalize")
         if self.tensor_parallel_size > 1:
             rows = ws.get("rows", L * tok, torch.float32)
@@ -436,6 +464,8 @@ class TriAttentionMethod(KVCompressionMethod):
             what.append("a keep index outside its request")
         if bits & N.DEV_BUDGET:
             what.append("a request shorter than kv_budget or its protected windows")
+        if bits & N.DEV_TIMEOUT:
+            what.append("a pipeline wait that timed out")
         return "TriAttention kernels rejected " + ", ".join(what)
 
 
