@@ -38,6 +38,7 @@ extern "C" {
 #define KVC_EALIGN (-71)      /* pointer or stride misaligned for the kernel */
 #define KVC_EUNSUPPORTED (-95) /* geometry not compiled (e.g. query group > 8) */
 #define KVC_ECUDA (-5)        /* the launch itself failed */
+#define KVC_ECAPACITY (-28)   /* request larger than a fixed, library-owned scratch */
 
 /* device error bits (OR-ed into *error_flag) */
 #define KVC_DEV_BLOCK_RANGE 1   /* a block id outside [0, num_blocks) */
@@ -231,6 +232,28 @@ int kvc_calibration_accumulate(const void* q, int dtype, int64_t n_tokens, int64
                                int heads, int head_dim, int rotary_dim, double* re_sum,
                                double* im_sum, double* abs_sum, double* pass_sum,
                                double* workspace, int64_t workspace_doubles, void* stream);
+
+/*
+ * Allocation-free calibration reduction.  No counterpart in the reference: it
+ * is an addition of this library for callers that cannot provide device
+ * memory -- a process whose GPU memory is already reserved (vLLM sizes the KV
+ * cache to the whole memory budget, so a later cudaMalloc may fail) or a
+ * foreign-language host that binds only this C ABI without a device allocator.
+ * Same inputs, outputs and results as kvc_calibration_accumulate; the chunk
+ * partials live in a library-owned static device array of
+ * KVC_CALIB_STATIC_SCRATCH_DOUBLES doubles (8 MiB), which every GPU that loads
+ * the library keeps until process exit.  Calls whose
+ * kvc_calibration_workspace_doubles() exceeds that return KVC_ECAPACITY
+ * without launching (about 69k tokens per call for 40 heads x head_dim 128).
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls on a device share the array: calls that overlap on the GPU race.
+ * No cudaMalloc/cudaFree or other allocating routine is called.
+ */
+#define KVC_CALIB_STATIC_SCRATCH_DOUBLES (1 << 20)
+int kvc_calibration_accumulate_noalloc(const void* q, int dtype, int64_t n_tokens, int64_t row_stride,
+                                       int heads, int head_dim, int rotary_dim, double* re_sum,
+                                       double* im_sum, double* abs_sum, double* pass_sum, void* stream);
 
 /*
  * Physical decode positions: out[i] = positions[i] - offsets[request_indices[i]].

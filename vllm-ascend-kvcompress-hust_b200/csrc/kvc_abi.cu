@@ -11,6 +11,7 @@ extern "C" const char* kvc_status_string(int status) {
     case KVC_EALIGN: return "pointer or stride misaligned for the kernel";
     case KVC_EUNSUPPORTED: return "geometry not supported by the compiled kernels";
     case KVC_ECUDA: return "CUDA launch failed";
+    case KVC_ECAPACITY: return "request exceeds the library's fixed static scratch capacity";
     default: return "unknown status";
   }
 }

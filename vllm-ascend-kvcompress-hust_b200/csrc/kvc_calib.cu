@@ -7,6 +7,8 @@
 // of tokens in fp32 (|q| = sqrt(re^2 + im^2) per element) and writes the chunk
 // partial; a second kernel adds the chunk partials in a fixed order in fp64
 // into the caller's running fp64 sums (deterministic, atomics-free).
+#include <mutex>
+
 #include "kvc_common.cuh"
 
 namespace kvc {
@@ -180,4 +182,58 @@ extern "C" int kvc_calibration_accumulate(const void* q, int dtype, int64_t n_to
   calib_finalize_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
       workspace, nchunk, a.cols, a.rope_cols, heads, F, P, V, re_sum, im_sum, abs_sum, pass_sum);
   return launch_status();
+}
+
+namespace kvc {
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant: chunk partials in library-owned static device memory
+// ---------------------------------------------------------------------------
+//
+// Some hosts cannot hand this library a device workspace: a process whose GPU
+// memory was reserved up front (vLLM sizes the KV cache to fill the memory
+// budget, so a later cudaMalloc can fail), or a foreign-language host that binds
+// only this C ABI and has no device allocator.  For them the chunk partials of
+// the calibration reduction live in one file-scope __device__ array that every
+// GPU loading the library keeps until process exit.  The array is shared by all
+// calls on a device: calls that overlap on the GPU (different streams or
+// threads without ordering) race on it.  Nothing in it must start at zero:
+// each call writes every partial it later reads.
+
+static __device__ __align__(256) double g_calib_scratch[KVC_CALIB_STATIC_SCRATCH_DOUBLES];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+// Device address of g_calib_scratch on the current device, resolved once per
+// device (host code must not use the symbol's name as a device pointer).
+int static_scratch(double** out) {
+  static std::mutex mu;
+  static double* ptrs[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return KVC_ECUDA;
+  std::lock_guard<std::mutex> lock(mu);
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_calib_scratch) != cudaSuccess || p == nullptr) return KVC_ECUDA;
+    ptrs[dev] = static_cast<double*>(p);
+  }
+  *out = ptrs[dev];
+  return KVC_OK;
+}
+
+}  // namespace
+}  // namespace kvc
+
+extern "C" int kvc_calibration_accumulate_noalloc(const void* q, int dtype, int64_t n_tokens, int64_t row_stride,
+                                                  int heads, int head_dim, int rotary_dim, double* re_sum,
+                                                  double* im_sum, double* abs_sum, double* pass_sum, void* stream) {
+  const int64_t need = kvc_calibration_workspace_doubles(n_tokens, heads, head_dim, rotary_dim);
+  if (need > KVC_CALIB_STATIC_SCRATCH_DOUBLES) return KVC_ECAPACITY;
+  double* scratch = nullptr;
+  const int rc = kvc::static_scratch(&scratch);
+  if (rc != KVC_OK) return rc;
+  return kvc_calibration_accumulate(q, dtype, n_tokens, row_stride, heads, head_dim, rotary_dim, re_sum, im_sum,
+                                    abs_sum, pass_sum, scratch, KVC_CALIB_STATIC_SCRATCH_DOUBLES, stream);
 }

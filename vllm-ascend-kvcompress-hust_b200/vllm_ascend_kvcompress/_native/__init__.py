@@ -16,7 +16,9 @@ ABI_VERSION = 1
 LIB_NAME = "libkvc_b200.so"
 
 KVC_OK = 0
-STATUS = {0: "ok", -22: "EINVAL", -14: "ENULL", -71: "EALIGN", -95: "EUNSUPPORTED", -5: "ECUDA"}
+STATUS = {0: "ok", -22: "EINVAL", -14: "ENULL", -71: "EALIGN", -95: "EUNSUPPORTED", -5: "ECUDA",
+          -28: "ECAPACITY"}
+CALIB_STATIC_SCRATCH_DOUBLES = 1 << 20
 DEV_BLOCK_RANGE, DEV_TOKEN_RANGE, DEV_BUDGET, DEV_TIMEOUT = 1, 2, 4, 8
 TENSOR_MAP_BYTES = 128
 BF16, FP16 = 0, 1
@@ -54,6 +56,8 @@ _SIGNATURES = {
     "kvc_calibration_accumulate": (
         c_int, [_P, c_int, c_int64, c_int64, c_int, c_int, c_int, _P, _P, _P, _P, _P, c_int64, _P]),
     "kvc_shift_positions": (c_int, [_P, _P, c_int, _P, c_int64, c_int64, _P, _P, _P]),
+    "kvc_calibration_accumulate_noalloc": (
+        c_int, [_P, c_int, c_int64, c_int64, c_int, c_int, c_int, _P, _P, _P, _P, _P]),
 }
 
 _lib: ctypes.CDLL | None = None
