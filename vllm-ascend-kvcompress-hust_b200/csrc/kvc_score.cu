@@ -391,8 +391,10 @@ __global__ void __launch_bounds__(256) head_stats_kernel(const float* __restrict
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int p0 = page_off[r], p1 = page_off[r + 1], T = tokens[r];
   const int span = kBlock / parts;  // tokens per partial
+  (void)L;
   const float2* part = reinterpret_cast<const float2*>(partial) + (int64_t)l * total_pages * parts * heads;
-  for (int hg = warp; hg < heads; hg += blockDim.x >> 5) {
+  const int hg = blockIdx.z * (blockDim.x >> 5) + warp;  // one warp per query head
+  if (hg < heads) {
     Moments m{0, 0, 0};
     for (int q = p0 * parts + lane; q < p1 * parts; q += 32) {
       const int n = min(span, T - (q - p0 * parts) * span);
@@ -439,13 +441,20 @@ __global__ void __launch_bounds__(256) normalize_kernel(const float* __restrict_
     return;
   }
   float acc = 0.f;
+  constexpr int U = 8;  // independent loads in flight per thread
   for (int l = 0; l < L; ++l) {
     const float* rl = raw + (int64_t)l * heads * tok_total + tok;
     const float* mu = mean + ((int64_t)l * R + r) * heads;
     const float* dn = den + ((int64_t)l * R + r) * heads;
     float z = -INFINITY;
-    for (int hg = 0; hg < heads; ++hg)
-      z = nan_max(z, __fdiv_rn(__ldg(rl + (int64_t)hg * tok_total) - __ldg(mu + hg), __ldg(dn + hg)));
+    for (int h0 = 0; h0 < heads; h0 += U) {
+      float x[U];
+#pragma unroll
+      for (int k = 0; k < U; ++k) x[k] = h0 + k < heads ? __ldg(rl + (int64_t)(h0 + k) * tok_total) : 0.f;
+#pragma unroll
+      for (int k = 0; k < U; ++k)
+        if (h0 + k < heads) z = nan_max(z, __fdiv_rn(x[k] - __ldg(mu + h0 + k), __ldg(dn + h0 + k)));
+    }
     if (rows) {
       rows[(int64_t)l * tok_total + tok] = z;
     } else if (l == 0) {
@@ -621,8 +630,8 @@ extern "C" int kvc_head_stats(const float* partial, int L, int R, int total_page
   KVC_CHECK_ARG(L > 0 && R >= 0 && heads > 0 && total_pages >= 0, KVC_EINVAL);
   KVC_CHECK_ARG(parts_per_page == 1 || parts_per_page == 4, KVC_EINVAL);
   if (R == 0) return KVC_OK;
-  head_stats_kernel<<<dim3(L, R), 256, 0, (cudaStream_t)stream>>>(partial, L, R, total_pages, parts_per_page, heads,
-                                                                  tokens, page_off, mean_out, var_out, denom_out);
+  head_stats_kernel<<<dim3(L, R, (heads + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
+      partial, L, R, total_pages, parts_per_page, heads, tokens, page_off, mean_out, var_out, denom_out);
   return launch_status();
 }
 

@@ -190,6 +190,12 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* map, int c
       : "memory");
 }
 
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
@@ -232,7 +238,8 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi, Fp16) {
   return d;
 }
 
-// m = |(kr, ki)| for the 8 elements of an A fragment, split into hi + lo halves.
+// m = |(kr, ki)| for the 8 elements of an A fragment, split into hi + lo halves
+// (packed fp32x2 arithmetic: two elements per instruction).
 template <class E>
 __device__ __forceinline__ void modulus_split(const uint32_t (&kr)[4], const uint32_t (&ki)[4], uint32_t (&hi)[4],
                                               uint32_t (&lo)[4]) {
@@ -240,11 +247,13 @@ __device__ __forceinline__ void modulus_split(const uint32_t (&kr)[4], const uin
   for (int i = 0; i < 4; ++i) {
     const float2 r = unpack2(kr[i], E{});
     const float2 m = unpack2(ki[i], E{});
-    const float m0 = sqrt_approx(r.x * r.x + m.x * m.x);
-    const float m1 = sqrt_approx(r.y * r.y + m.y * m.y);
-    hi[i] = pack2(m0, m1, E{});
+    float2 sq = __fmul2_rn(r, r);
+    sq = __ffma2_rn(m, m, sq);
+    const float2 mod = make_float2(sqrt_approx(sq.x), sqrt_approx(sq.y));
+    hi[i] = pack2(mod.x, mod.y, E{});
     const float2 h = unpack2(hi[i], E{});
-    lo[i] = pack2(m0 - h.x, m1 - h.y, E{});
+    const float2 d = __ffma2_rn(h, make_float2(-1.f, -1.f), mod);
+    lo[i] = pack2(d.x, d.y, E{});
   }
 }
 
@@ -276,9 +285,11 @@ struct TcGeom {
   static constexpr int S = frag_steps(F, P);
   static constexpr int kBoxes = D / kBoxElems;
   static constexpr int kStageBytes = kBoxes * kBoxBytes;
-  static constexpr int kStages = D <= 128 ? 3 : 2;
-  static constexpr int kSmem = kStages * kStageBytes + 1024 + 64;
-  static constexpr int kMinBlocks = D <= 128 ? 2 : 1;
+  static constexpr int kWBytes = S * 32 * 16;  // B fragments of one (request, layer, head)
+  static constexpr int kStages = D <= 64 ? 3 : D <= 128 ? 2 : 3;
+  static constexpr int kMinBlocks = D <= 128 ? 3 : 1;
+  // stages | W buffer | full/empty/wfull/wfree barriers | unit metadata
+  static constexpr int kSmem = 1024 + kStages * kStageBytes + kWBytes + 8 * (2 * kStages + 2) + 32 * kStages;
 };
 
 // Shared-memory byte address of 16-element column group `col16` (dims col16*16 ..)
@@ -291,128 +302,172 @@ __device__ __forceinline__ uint32_t frag_addr(uint32_t stage, int row0, int dim0
   return stage + box * kBoxBytes + row * 128 + ((chunk ^ (row & 7)) << 4);
 }
 
+// Unit metadata the producer hands to the consumers with each stage.
+struct UnitMeta {
+  int p, h, lg, valid, wgen, end;
+};
+
+// Pipeline (per CTA): one producer lane resolves its contiguous range of
+// (layer, head, page) units, publishes each unit's metadata and issues the
+// page's TMA boxes into a ring stage (full/empty mbarriers).  The B-operand
+// fragments W of the unit's (request, layer, head) live in one shared buffer:
+// when they change ("generation" n), the producer first publishes the stage,
+// then waits until every consumer warp has released generation n-1 (wfree),
+// and bulk-copies the new fragments (wfull).  Consumers thus never hold W in
+// registers, which leaves room for three CTAs per SM.
 template <int F, int P, class E>
 __global__ void __launch_bounds__(kTcThreads, TcGeom<F, P>::kMinBlocks) score_tc_kernel(const __grid_constant__ TcArgs a) {
   using Gm = TcGeom<F, P>;
-  constexpr int S = Gm::S;
   constexpr int KF = F / 16;
   constexpr int KP = P / 16;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base + Gm::kStages * Gm::kStageBytes);
+  const uint4* wsm = reinterpret_cast<const uint4*>(base + Gm::kStages * Gm::kStageBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + Gm::kStages * Gm::kStageBytes + Gm::kWBytes);
+  UnitMeta* meta = reinterpret_cast<UnitMeta*>(bars + 2 * Gm::kStages + 2);
   const uint32_t stage0 = smem_u32(base);
+  const uint32_t wbuf = smem_u32(wsm);
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + Gm::kStages);
+  const uint32_t wfull = smem_u32(bars + 2 * Gm::kStages), wfree = wfull + 8;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < Gm::kStages; ++s) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, kTcConsumers);
     }
+    mbar_init(wfull, 1);
+    mbar_init(wfree, kTcConsumers);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-
-  const int64_t per = (a.units + gridDim.x - 1) / gridDim.x;
-  const int64_t u0 = (int64_t)blockIdx.x * per;
-  const int64_t u1 = min64(a.units, u0 + per);
   const int heads = a.kvh * a.G;
 
   if (warp == kTcConsumers) {
-    // ---------------- producer: one elected lane issues the TMA tiles ----------
-    if (lane == 0) {
-      uint32_t it = 0;
-      for (int64_t u = u0; u < u1; ++u) {
-        const int p = (int)(u % a.total_pages);
-        const int h = (int)((u / a.total_pages) % a.kvh);
-        const int l = (int)(u / ((int64_t)a.total_pages * a.kvh));
-        const int r = request_of_page(a.page_off, a.R, p);
-        const int pl = p - __ldg(a.page_off + r);
-        const int64_t blk = __ldg(a.src_blocks + __ldg(a.src_block_off + r) + pl);
-        if (blk < 0 || blk >= a.num_blocks) continue;  // consumers skip the same unit
-        const int s = it % Gm::kStages;
-        const uint32_t ph = (it / Gm::kStages) & 1;
-        if (!mbar_wait(empty0 + 8 * s, ph ^ 1, a.error_flag)) break;
-        mbar_expect_tx(full0 + 8 * s, Gm::kStageBytes);
-#pragma unroll
-        for (int b = 0; b < Gm::kBoxes; ++b)
-          tma_load_4d(stage0 + s * Gm::kStageBytes + b * kBoxBytes, &a.maps[l], b * kBoxElems, h, 0, (int)blk,
-                      full0 + 8 * s);
-        ++it;
+    // ---------------- producer -------------------------------------------------
+    if (lane != 0) return;
+    const int64_t per = (a.units + gridDim.x - 1) / gridDim.x;
+    const int64_t u0 = (int64_t)blockIdx.x * per;
+    const int64_t u1 = min64(a.units, u0 + per);
+    uint32_t it = 0;
+    int r = 0, cur_key = -1, gen = -1;
+    bool ok = true;
+    for (int64_t u = u0; u < u1 && ok; ++u) {
+      const int p = (int)(u % a.total_pages);
+      const int h = (int)((u / a.total_pages) % a.kvh);
+      const int l = (int)(u / ((int64_t)a.total_pages * a.kvh));
+      if (u == u0 || p == 0) r = request_of_page(a.page_off, a.R, p);
+      while (__ldg(a.page_off + r + 1) <= p) ++r;  // units advance page by page
+      const int pl = p - __ldg(a.page_off + r);
+      const int64_t blk = __ldg(a.src_blocks + __ldg(a.src_block_off + r) + pl);
+      if (blk < 0 || blk >= a.num_blocks) {
+        raise_flag(a.error_flag, KVC_DEV_BLOCK_RANGE);
+        continue;
       }
-      // drain: every issued tile must have landed before the CTA may exit
-      for (uint32_t k = 0; k < Gm::kStages && k < it; ++k) {
-        const uint32_t j = it - 1 - k;
-        mbar_wait(full0 + 8 * (j % Gm::kStages), (j / Gm::kStages) & 1, a.error_flag);
+      const int lg = a.layer0 + l;
+      const int key = (r * a.L_total + lg) * a.kvh + h;
+      const bool new_w = key != cur_key;
+      if (new_w) {
+        cur_key = key;
+        ++gen;
+      }
+      const int s = it % Gm::kStages;
+      if (!mbar_wait(empty0 + 8 * s, ((it / Gm::kStages) & 1) ^ 1, a.error_flag)) {
+        ok = false;
+        break;
+      }
+      meta[s] = UnitMeta{p, h, lg, min(kBlock, __ldg(a.tokens + r) - pl * kBlock), gen, 0};
+      mbar_expect_tx(full0 + 8 * s, Gm::kStageBytes);
+#pragma unroll
+      for (int b = 0; b < Gm::kBoxes; ++b)
+        tma_load_4d(stage0 + s * Gm::kStageBytes + b * kBoxBytes, &a.maps[l], b * kBoxElems, h, 0, (int)blk,
+                    full0 + 8 * s);
+      ++it;
+      if (new_w) {
+        // the consumers release generation gen-1 when they reach this stage
+        if (gen > 0 && !mbar_wait(wfree, (gen - 1) & 1, a.error_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(wfull, Gm::kWBytes);
+        bulk_load(wbuf, a.frag + (int64_t)key * Gm::S * 32, Gm::kWBytes, wfull);
       }
     }
+    if (ok) {  // sentinel stage: tells the consumers the range is done
+      const int s = it % Gm::kStages;
+      if (mbar_wait(empty0 + 8 * s, ((it / Gm::kStages) & 1) ^ 1, a.error_flag)) {
+        meta[s].end = 1;
+        mbar_arrive(full0 + 8 * s);
+        ++it;
+      }
+    }
+    // drain: every issued copy must have landed before the CTA may exit
+    for (uint32_t k = 0; k < Gm::kStages && k < it; ++k) {
+      const uint32_t j = it - 1 - k;
+      mbar_wait(full0 + 8 * (j % Gm::kStages), (j / Gm::kStages) & 1, a.error_flag);
+    }
+    if (gen >= 0) mbar_wait(wfull, gen & 1, a.error_flag);
     return;
   }
 
   // ---------------- consumers: 4 warps x 32 tokens of each 128-token tile ----
-  uint4 w[S];
-  int cur_key = -1;
-  uint32_t it = 0;
-  for (int64_t u = u0; u < u1; ++u) {
-    const int p = (int)(u % a.total_pages);
-    const int h = (int)((u / a.total_pages) % a.kvh);
-    const int l = (int)(u / ((int64_t)a.total_pages * a.kvh));
-    const int r = request_of_page(a.page_off, a.R, p);
-    const int pl = p - __ldg(a.page_off + r);
-    const int valid = min(kBlock, __ldg(a.tokens + r) - pl * kBlock);
-    const int64_t blk = __ldg(a.src_blocks + __ldg(a.src_block_off + r) + pl);
-    if (blk < 0 || blk >= a.num_blocks) {
-      if (warp == 0 && lane == 0) raise_flag(a.error_flag, KVC_DEV_BLOCK_RANGE);
-      continue;
-    }
-    const int lg = a.layer0 + l;
-    const int key = (r * a.L_total + lg) * a.kvh + h;
-    if (key != cur_key) {
-      const uint4* src = a.frag + (int64_t)key * S * 32 + lane;
-#pragma unroll
-      for (int s = 0; s < S; ++s) w[s] = __ldg(src + s * 32);
-      cur_key = key;
-    }
+  int cur_gen = -1;
+  // per-lane byte offsets of the ldmatrix rows of this warp's two m16 tiles
+  for (uint32_t it = 0;; ++it) {
     const int s = it % Gm::kStages;
-    const uint32_t ph = (it / Gm::kStages) & 1;
-    ++it;
-    if (!mbar_wait(full0 + 8 * s, ph, a.error_flag)) return;
+    if (!mbar_wait(full0 + 8 * s, (it / Gm::kStages) & 1, a.error_flag)) return;
+    const UnitMeta mu = meta[s];
+    if (mu.end) break;
+    if (mu.wgen != cur_gen) {
+      __syncwarp();
+      if (cur_gen >= 0 && lane == 0) mbar_arrive(wfree);  // done with the previous fragments
+      if (!mbar_wait(wfull, mu.wgen & 1, a.error_flag)) return;
+      cur_gen = mu.wgen;
+    }
     const uint32_t stage = stage0 + s * Gm::kStageBytes;
+    const uint4* wl = wsm + lane;
 
     float y[2][4];
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt) {
       const int row0 = warp * 32 + mt * 16;
-      float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+      // independent accumulator chains: kr, ki, modulus (and pass), hi/lo column halves
+      float ar0[4] = {}, ar1[4] = {}, ai0[4] = {}, ai1[4] = {}, am0[4] = {}, am1[4] = {};
 #pragma unroll
       for (int j = 0; j < KF; ++j) {
         uint32_t kr[4], ki[4], mh[4], ml[4];
         ldsm_x4(frag_addr(stage, row0, 16 * j, lane), kr);
         ldsm_x4(frag_addr(stage, row0, F + 16 * j, lane), ki);
-        mma16816<E>(c0, kr, w[j].x, w[j].y);
-        mma16816<E>(c1, kr, w[j].z, w[j].w);
-        mma16816<E>(c0, ki, w[KF + j].x, w[KF + j].y);
-        mma16816<E>(c1, ki, w[KF + j].z, w[KF + j].w);
+        const uint4 wa = wl[j * 32], wb = wl[(KF + j) * 32];
+        mma16816<E>(ar0, kr, wa.x, wa.y);
+        mma16816<E>(ar1, kr, wa.z, wa.w);
+        mma16816<E>(ai0, ki, wb.x, wb.y);
+        mma16816<E>(ai1, ki, wb.z, wb.w);
         modulus_split<E>(kr, ki, mh, ml);
-        mma16816<E>(c0, mh, w[2 * KF + j].x, w[2 * KF + j].y);
-        mma16816<E>(c1, mh, w[2 * KF + j].z, w[2 * KF + j].w);
-        mma16816<E>(c0, ml, w[3 * KF + j].x, w[3 * KF + j].y);
+        const uint4 we = wl[(2 * KF + j) * 32], wf = wl[(3 * KF + j) * 32];
+        mma16816<E>(am0, mh, we.x, we.y);
+        mma16816<E>(am1, mh, we.z, we.w);
+        mma16816<E>(am0, ml, wf.x, wf.y);
       }
+      float ap0[4] = {}, ap1[4] = {};
 #pragma unroll
       for (int j = 0; j < KP; ++j) {
         uint32_t kp[4];
         ldsm_x4(frag_addr(stage, row0, 2 * F + 16 * j, lane), kp);
-        mma16816<E>(c0, kp, w[4 * KF + j].x, w[4 * KF + j].y);
-        mma16816<E>(c1, kp, w[4 * KF + j].z, w[4 * KF + j].w);
+        const uint4 wp = wl[(4 * KF + j) * 32];
+        mma16816<E>(ap0, kp, wp.x, wp.y);
+        mma16816<E>(ap1, kp, wp.z, wp.w);
       }
 #pragma unroll
-      for (int i = 0; i < 4; ++i) y[mt][i] = c0[i] + c1[i];
+      for (int i = 0; i < 4; ++i)
+        y[mt][i] = ((ar0[i] + ar1[i]) + (ai0[i] + ai1[i])) + ((am0[i] + am1[i]) + (ap0[i] + ap1[i]));
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty0 + 8 * s);
 
     // ---- epilogue: raw scores and the quarter-page moments of each query head
     // lane holds heads g = 2*(lane%4) + {0,1} for tokens warp*32 + {0,8,16,24} + lane/4
-    const int nq = max(0, min(32, valid - warp * 32));
+    const int nq = max(0, min(32, mu.valid - warp * 32));
+    const float inv_nq = nq > 0 ? __frcp_rn((float)nq) : 0.f;
 #pragma unroll
     for (int gi = 0; gi < 2; ++gi) {
       const int g = 2 * (lane & 3) + gi;
@@ -420,27 +475,27 @@ __global__ void __launch_bounds__(kTcThreads, TcGeom<F, P>::kMinBlocks) score_tc
       bool ok[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int mt = i >> 1, half = i & 1;
-        const int t = warp * 32 + mt * 16 + half * 8 + (lane >> 2);
-        vals[i] = y[mt][half * 2 + gi];
-        ok[i] = t < valid && g < a.G;
+        const int t = warp * 32 + (i >> 1) * 16 + (i & 1) * 8 + (lane >> 2);
+        vals[i] = y[i >> 1][(i & 1) * 2 + gi];
+        ok[i] = t < mu.valid && g < a.G;
       }
       float sum = 0.f;
 #pragma unroll
       for (int i = 0; i < 4; ++i) sum += ok[i] ? vals[i] : 0.f;
 #pragma unroll
       for (int o = 4; o < 32; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      const float mu = nq > 0 ? sum / (float)nq : 0.f;
+      // centring value for M2 only: any value near the mean keeps Chan's combination exact
+      const float mean = sum * inv_nq;
       float m2 = 0.f;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const float d = vals[i] - mu;
+        const float d = vals[i] - mean;
         m2 += ok[i] ? d * d : 0.f;
       }
 #pragma unroll
       for (int o = 4; o < 32; o <<= 1) m2 += __shfl_xor_sync(0xffffffffu, m2, o);
       if (g < a.G) {
-        float* row = a.raw + ((int64_t)lg * heads + h * a.G + g) * a.tok_total + (int64_t)p * kBlock;
+        float* row = a.raw + ((int64_t)mu.lg * heads + mu.h * a.G + g) * a.tok_total + (int64_t)mu.p * kBlock;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int t = warp * 32 + (i >> 1) * 16 + (i & 1) * 8 + (lane >> 2);
@@ -448,7 +503,7 @@ __global__ void __launch_bounds__(kTcThreads, TcGeom<F, P>::kMinBlocks) score_tc
         }
         if (lane < 4) {
           float2* out = reinterpret_cast<float2*>(a.partial) +
-                        (((int64_t)lg * a.total_pages + p) * 4 + warp) * heads + h * a.G + g;
+                        (((int64_t)mu.lg * a.total_pages + mu.p) * 4 + warp) * heads + mu.h * a.G + g;
           *out = make_float2(sum, m2);
         }
       }
