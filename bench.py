@@ -203,7 +203,7 @@ def reference_arm(args) -> None:
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    w = W.config1(stride=args.stride, num_seqs=args.seqs, num_layers=args.layers)
+    w = make_workload(args)
     seq = sorted(w.compressed(), key=lambda i: w.lengths[i])[len(w.compressed()) // 2]  # median-length sequence
     budget_s = 150.0
     t0 = time.perf_counter()
@@ -215,7 +215,7 @@ def reference_arm(args) -> None:
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
         "warmup": 1, "ms_per_step": info["seconds"] * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) BF16 K/V, random calibration stats)",
-        "config": config_dict(w, world),
+        "config": config_dict(w, world, distinct_layers(args, w)),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": info["threads"], "kind": "port",
                          "sample": info["sample"]},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -223,12 +223,39 @@ def reference_arm(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def config_dict(w: W.Workload, world: int) -> dict:
+WORKLOAD_TEXT = {
+    "config0": "config0: CPU-runnable reference op, 1 layer, 40 q / 8 kv heads, head_dim 128, 4 seqs "
+               "{{1000, 2500, 4096, 6000}}, kv_budget 2048, V3 prefix 4 / recent 128",
+    "config1": "config1: Qwen2.5-14B-shaped ragged batch, {layers} layers, 40 q / 8 kv heads, head_dim 128, "
+               "{seqs} seqs U[4096,32768] (seed 1), kv_budget 4608, V3 prefix 128 / recent 512 / 8 segments",
+    "config2": "config2: Qwen3.5-35B-A3B-shaped full-attention layers, 10 layers, 16 q / 2 kv heads, head_dim 256, "
+               "partial RoPE 64, 2048-token pages, 16 seqs U[8192,53248] (seed 2), kv_budget 4608, stride 2",
+    "config4": "config4: 48 layers ({distinct} distinct caches aliased round-robin), 40 q / 8 kv heads, head_dim 128, "
+               "{seqs} seqs U[2048,65536] (seed 4), kv_budget 4608, stride 8",
+}
+
+
+def make_workload(args) -> W.Workload:
+    if args.config == 0:
+        return W.config0()
+    if args.config == 2:
+        return W.config2()
+    if args.config == 4:
+        return W.config4(num_seqs=args.seqs if args.seqs != 32 else 128, stride=args.stride)
+    return W.config1(stride=args.stride, num_seqs=args.seqs, num_layers=args.layers)
+
+
+def distinct_layers(args, w: W.Workload) -> int:
+    if args.distinct_layers:
+        return min(args.distinct_layers, w.geometry.num_layers)
+    return 5 if args.config == 4 else w.geometry.num_layers
+
+
+def config_dict(w: W.Workload, world: int, distinct: int | None = None) -> dict:
     o = w.options
     return {
-        "workload": f"config1: Qwen2.5-14B-shaped ragged batch, {w.geometry.num_layers} layers, 40 q / 8 kv heads, "
-                    f"head_dim 128, {len(w.lengths)} seqs U[4096,32768] (seed 1), kv_budget 4608, "
-                    "V3 prefix 128 / recent 512 / 8 segments",
+        "workload": WORKLOAD_TEXT[w.name].format(layers=w.geometry.num_layers, seqs=len(w.lengths),
+                                                 distinct=distinct or w.geometry.num_layers),
         "global_batch": len(w.lengths), "compressed_sequences": len(w.compressed()),
         "compressed_tokens": w.total_compressed_tokens(), "layers": w.geometry.num_layers,
         "score_layer_stride": o.score_layer_stride, "kv_budget": o.kv_budget,
@@ -254,15 +281,14 @@ def b200_arm(args) -> None:
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
         group = dist.group.WORLD
-    w = W.config1(stride=args.stride, num_seqs=args.seqs, num_layers=args.layers)
+    w = make_workload(args)
     geo = w.geometry
     if geo.num_kv_heads % world:
         raise SystemExit(f"{geo.num_kv_heads} KV heads cannot be sharded over {world} ranks")
     kvh = geo.num_kv_heads // world
-    caches = []
-    for layer in range(geo.num_layers):
-        k, v = W.kv_pages(w, layer * world + rank, kv_heads=kvh, device=dev)
-        caches.append((k, v))
+    nd = distinct_layers(args, w)
+    physical = [W.kv_pages(w, layer * world + rank, kv_heads=kvh, device=dev) for layer in range(nd)]
+    caches = [physical[layer % nd] for layer in range(geo.num_layers)]
     torch.cuda.synchronize()
     with tempfile.TemporaryDirectory() as d:
         m = W.b200_method(w, caches, W.write_stats_file(w, d), tp_size=world, tp_group=group, tp_rank=rank,
@@ -358,7 +384,7 @@ def b200_arm(args) -> None:
         score_gbs = ab["score"] / (score_ms * 1e-3) / 1e9
         traffic = None
         tf = ROOT / "profiles" / "traffic.json"
-        if tf.is_file():
+        if tf.is_file() and args.config == 1 and args.seqs == 32 and args.layers == 48:
             traffic = json.loads(tf.read_text()).get("compact_kernel_bytes_per_launch_config1")
         launches_per_step = 6 + (1 if world > 1 else 0)
         step_bytes = sum(ab.values())
@@ -367,7 +393,7 @@ def b200_arm(args) -> None:
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded N(0,1) BF16 K/V, random calibration stats)",
-            "config": config_dict(w, world),
+            "config": config_dict(w, world, nd),
             "roofline": {"bound": "hbm", "kernel": "kvc compact (paged K/V gather-copy, all layers)",
                          "achieved": comp_gbs, "peak": peak, "unit": "GB/s", "frac": comp_gbs / peak,
                          "traffic": traffic, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
@@ -386,7 +412,7 @@ def b200_arm(args) -> None:
         }
         if world == 1 and not args.no_cpu_baseline:
             seq = sorted(w.compressed(), key=lambda i: w.lengths[i])[len(w.compressed()) // 2]
-            v, info = run_cpu_sample(w, seq)
+            v, info = run_cpu_sample(w, seq, distinct_layers=min(8, geo.num_layers))
             line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": info["threads"], "kind": "port",
                                     "sample": info["sample"]}
         print(json.dumps(line), flush=True)
@@ -395,6 +421,63 @@ def b200_arm(args) -> None:
 
         dist.barrier()
         dist.destroy_process_group()
+
+
+def calib_arm(args) -> None:
+    """Config 3: calibration reduction of 48 layers x 64 x 8192 pre-RoPE queries (40 heads x 128)."""
+    from vllm_ascend_kvcompress.methods.triattention import kernels as K
+
+    rank, world, local = dist_env()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    heads, hd, rot = 40, 128, 128
+    n_seq, seq_len = 64, 8192
+    layers = args.layers if args.layers != 48 else 48
+    n_tok = n_seq * seq_len
+    need = K.calibration_workspace_doubles(n_tok, heads, hd, rot)
+    ws = torch.empty(need, dtype=torch.float64, device=dev)
+    z = lambda: torch.zeros(heads, rot // 2, dtype=torch.float64, device=dev)
+    total_ms, worst = 0.0, 0.0
+    for layer in range(layers):
+        q = W.calibration_queries(layer, n_seq, seq_len, heads, hd, device=dev)
+        re, im, ab = z(), z(), z()
+        for _ in range(2):  # warm-up pass (layer 0) then the timed pass
+            re.zero_(); im.zero_(); ab.zero_()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            K.calibration_accumulate(q, heads, hd, rot, re, im, ab, None, ws)
+            b.record()
+            torch.cuda.synchronize()
+            if layer > 0:
+                break
+        total_ms += a.elapsed_time(b)
+        if layer == 0:  # parity against an fp64 reduction of the same tensor
+            v = q.view(-1, heads, hd).double()
+            ref = (v[..., :rot // 2].sum(0), v[..., rot // 2:rot].sum(0),
+                   torch.sqrt(v[..., :rot // 2].square() + v[..., rot // 2:rot].square()).sum(0))
+            mean_abs = v.abs().mean().item()
+            for g, r in zip((re, im, ab), ref):
+                worst = max(worst, ((g - r).abs().max() / n_tok).item() / max(r.abs().max().item() / n_tok, mean_abs))
+            del v
+        del q
+    tokens = layers * n_tok
+    bytes_ = tokens * heads * hd * 2.0
+    peak, kind = peaks()
+    gbs = bytes_ / (total_ms * 1e-3) / 1e9
+    print(json.dumps({
+        "metric": "calibration query tokens reduced/s (config 3)", "value": tokens / (total_ms * 1e-3),
+        "unit": "tokens/s", "n_gpus": 1, "steps": layers, "warmup": 1, "ms_per_step": total_ms / layers,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic pre-RoPE queries q ~ N(mu_h, 1), mu_h ~ N(0, 0.5), BF16",
+        "config": {"workload": f"config3: calibration reduction, {layers} layers x {n_seq} x {seq_len} tokens, "
+                               f"{heads} heads x head_dim {hd}", "layers": layers, "tokens_per_layer": n_tok},
+        "roofline": {"bound": "hbm", "kernel": "kvc calibration partial + finalize", "achieved": gbs, "peak": peak,
+                     "unit": "GB/s", "frac": gbs / peak, "traffic": None, "peak_source": kind},
+        "parity_max_rel_err_vs_fp64": worst,
+    }), flush=True)
 
 
 def main() -> None:
@@ -407,11 +490,17 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seqs", type=int, default=32, help="sequences (32 = config 1; smaller only for profiling)")
     ap.add_argument("--layers", type=int, default=48, help="layers (48 = config 1; smaller only for profiling)")
+    ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4],
+                    help="benchmark-specification configuration (1 = the headline line)")
+    ap.add_argument("--distinct-layers", type=int, default=0,
+                    help="physical caches aliased round-robin onto the layers (0 = all distinct; config 4 uses 5)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3
     if args.impl == "reference":
         reference_arm(args)
+    elif args.config == 3:
+        calib_arm(args)
     else:
         b200_arm(args)
 
