@@ -386,7 +386,7 @@ def b200_arm(args) -> None:
         tf = ROOT / "profiles" / "traffic.json"
         if tf.is_file() and args.config == 1 and args.seqs == 32 and args.layers == 48:
             traffic = json.loads(tf.read_text()).get("compact_kernel_bytes_per_launch_config1")
-        launches_per_step = 6 + (1 if world > 1 else 0)
+        launches_per_step = 7  # prepare, score, head_stats, normalize, aggregate_rows, select, compact
         step_bytes = sum(ab.values())
         line = {
             "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": args.steps,

@@ -94,7 +94,8 @@ int kvc_prepare_score_coefficients(const float* omega, const float* offsets, int
  *   coef         output of kvc_prepare_score_coefficients (same aggregation).
  *   q_pass_t     [L][kvh][head_dim-rotary_dim][G] fp32 (transposed q_pass_mean),
  *                NULL for full RoPE.
- *   raw_out      [L][kvh*G][total_pages*128] fp32.
+ *   raw_out      [L][total_pages][kvh*G][128] fp32 (page-major: one page's
+ *                scores of every query head are one contiguous block).
  *   partial_out  [L][total_pages][kvh*G][2] fp32: (page sum, page sum of
  *                squared deviations from the page mean).
  */
@@ -149,11 +150,12 @@ int kvc_head_stats(const float* partial, int num_layers, int num_requests, int t
                    float* mean_out, float* var_out, float* denom_out, void* stream);
 
 /*
- * Normalise (z = (raw - mean) / denom), max over the local query heads, then
- * either write one row per scoring layer (rows_out [L][total_pages*128], the
- * tensor-parallel all-reduce input) or, when rows_out is NULL, reduce the
- * layers (sum then / L, or max) and finalise (NaN -> -inf, +inf -> 1e30) into
- * agg_out [total_pages*128].
+ * Normalise (z = (raw - mean) / denom) and take the max over the local query
+ * heads, one row per scoring layer: rows_out [L][total_pages*128] (required;
+ * also the tensor-parallel all-reduce input).  When agg_out is non-NULL the
+ * layers are then reduced (sequential sum then / L, or max) and finalised
+ * (NaN -> -inf, +inf -> 1e30) into agg_out [total_pages*128]
+ * (kvc_aggregate_rows on the same stream).
  * Replaces aggregate_normalized_scores (methods/triattention/kernels.py:407-437),
  * TriAttentionMethod._aggregate_torch (methods/triattention/method.py:477-503)
  * and the finalisation at methods/triattention/method.py:463-467.

@@ -53,8 +53,10 @@ def test_pipeline_matches_reference_golden(name, scorer, tmp_path, monkeypatch):
     raw, mean, var, agg = (t.detach().cpu() for t in m.last_stats)
     offs = page_offsets(w, idx)
     heads = m.local_kv_heads * m.group
-    tok_total = raw.numel() // (m.scoring_layer_count * heads)
-    raw = raw.view(m.scoring_layer_count, heads, tok_total)
+    pages = raw.numel() // (m.scoring_layer_count * heads * 128)
+    # raw scores are page-major: [layer][page][query head][128 tokens]
+    raw = raw.view(m.scoring_layer_count, pages, heads, 128).permute(0, 2, 1, 3).reshape(
+        m.scoring_layer_count, heads, pages * 128)
     for row, i in enumerate(idx):
         t = w.lengths[i]
         g_agg = torch.from_numpy(arrays[f"{name}/r{i}/agg"])

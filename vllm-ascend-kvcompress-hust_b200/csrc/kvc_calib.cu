@@ -24,6 +24,14 @@ struct CalibArgs {
   double* ws;  // [nchunk][cols][3V]
 };
 
+// |q| of one frequency pair (hardware square root: within 2 ulp of the
+// correctly rounded value, far inside the statistics' tolerance)
+__device__ __forceinline__ float modulus(float re, float im) {
+  float y;
+  asm("sqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(fmaf(re, re, im * im)));
+  return y;
+}
+
 template <int V, class E>
 __device__ __forceinline__ void load_vals(const uint16_t* p, float (&x)[V]) {
   if constexpr (V == 8) {
@@ -39,11 +47,13 @@ __device__ __forceinline__ void load_vals(const uint16_t* p, float (&x)[V]) {
 }
 
 template <int V, class E>
-__global__ void __launch_bounds__(kCalibThreads) calib_partial_kernel(const __grid_constant__ CalibArgs a) {
+__global__ void __launch_bounds__(1024) calib_partial_kernel(const __grid_constant__ CalibArgs a) {
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
   if (col >= a.cols) return;
-  const int64_t t0 = (int64_t)blockIdx.y * kCalibChunk;
-  const int64_t t1 = min64(a.n_tok, t0 + kCalibChunk);
+  // balanced contiguous token ranges, one per CTA row (gridDim.y <= chunks)
+  const int64_t span = (a.n_tok + gridDim.y - 1) / gridDim.y;
+  const int64_t t0 = (int64_t)blockIdx.y * span;
+  const int64_t t1 = min64(a.n_tok, t0 + span);
   double* out = a.ws + ((int64_t)blockIdx.y * a.cols + col) * 3 * V;
   if (col < a.rope_cols) {
     const int per = a.F / V;
@@ -52,7 +62,25 @@ __global__ void __launch_bounds__(kCalibThreads) calib_partial_kernel(const __gr
     float re[V], im[V], ab[V];
 #pragma unroll
     for (int j = 0; j < V; ++j) re[j] = im[j] = ab[j] = 0.f;
-    for (int64_t t = t0; t < t1; ++t) {
+    constexpr int U = 4;  // tokens whose loads are in flight together
+    int64_t t = t0;
+    for (; t + U <= t1; t += U) {
+      float xr[U][V], xi[U][V];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        load_vals<V, E>(base + (t + u) * a.row_stride, xr[u]);
+        load_vals<V, E>(base + (t + u) * a.row_stride + a.F, xi[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+          re[j] += xr[u][j];
+          im[j] += xi[u][j];
+          ab[j] += modulus(xr[u][j], xi[u][j]);
+        }
+    }
+    for (; t < t1; ++t) {
       float xr[V], xi[V];
       load_vals<V, E>(base + t * a.row_stride, xr);
       load_vals<V, E>(base + t * a.row_stride + a.F, xi);
@@ -60,7 +88,7 @@ __global__ void __launch_bounds__(kCalibThreads) calib_partial_kernel(const __gr
       for (int j = 0; j < V; ++j) {
         re[j] += xr[j];
         im[j] += xi[j];
-        ab[j] += sqrtf(xr[j] * xr[j] + xi[j] * xi[j]);
+        ab[j] += modulus(xr[j], xi[j]);
       }
     }
 #pragma unroll
@@ -77,7 +105,18 @@ __global__ void __launch_bounds__(kCalibThreads) calib_partial_kernel(const __gr
     float s[V];
 #pragma unroll
     for (int j = 0; j < V; ++j) s[j] = 0.f;
-    for (int64_t t = t0; t < t1; ++t) {
+    constexpr int U = 4;
+    int64_t t = t0;
+    for (; t + U <= t1; t += U) {
+      float x[U][V];
+#pragma unroll
+      for (int u = 0; u < U; ++u) load_vals<V, E>(base + (t + u) * a.row_stride, x[u]);
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int j = 0; j < V; ++j) s[j] += x[u][j];
+    }
+    for (; t < t1; ++t) {
       float x[V];
       load_vals<V, E>(base + t * a.row_stride, x);
 #pragma unroll
@@ -88,14 +127,17 @@ __global__ void __launch_bounds__(kCalibThreads) calib_partial_kernel(const __gr
   }
 }
 
-// out element e of kind k (0 re, 1 im, 2 abs, 3 pass) <- sum over chunks
+// out element e of kind k (0 re, 1 im, 2 abs, 3 pass) <- sum over the partial
+// rows: one warp per element, lanes take every 32nd row, fixed-order fp64
+// shuffle tree (deterministic).
 __global__ void __launch_bounds__(256) calib_finalize_kernel(const double* __restrict__ ws, int64_t nchunk, int cols,
                                                              int rope_cols, int H, int F, int P, int V,
                                                              double* re_sum, double* im_sum, double* abs_sum,
                                                              double* pass_sum) {
   const int64_t rope_elems = (int64_t)H * F;
   const int64_t total = 3 * rope_elems + (int64_t)H * P;
-  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t e = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
   if (e >= total) return;
   int col, slot;
   double* dst;
@@ -114,8 +156,10 @@ __global__ void __launch_bounds__(256) calib_finalize_kernel(const double* __res
     dst = pass_sum + i;
   }
   double acc = 0.0;
-  for (int64_t c = 0; c < nchunk; ++c) acc += ws[((int64_t)c * cols + col) * 3 * V + slot];
-  *dst += acc;
+  for (int64_t c = lane; c < nchunk; c += 32) acc += ws[((int64_t)c * cols + col) * 3 * V + slot];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) *dst += acc;
 }
 
 inline int calib_vec(int F, int P, int64_t row_stride, const void* q) {
@@ -165,11 +209,21 @@ extern "C" int kvc_calibration_accumulate(const void* q, int dtype, int64_t n_to
   a.rope_cols = heads * (F / V);
   a.cols = a.rope_cols + heads * (P / V);
   a.ws = workspace;
-  const int64_t nchunk = (n_tokens + kCalibChunk - 1) / kCalibChunk;
+  int64_t nchunk = (n_tokens + kCalibChunk - 1) / kCalibChunk;  // upper bound of the partial rows
+  // one CTA spans all columns of a token range where possible; the ranges are
+  // sized so that the grid is one full wave of resident CTAs (no tail wave)
+  const int threads = std::min(1024, (a.cols + 31) / 32 * 32);
+  const int gx = (a.cols + threads - 1) / threads;
+  int per_sm = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, calib_partial_kernel<8, Bf16>, threads, 0) !=
+          cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  const int64_t wave = std::max<int64_t>(1, (int64_t)sm_count() * per_sm / gx);
+  nchunk = std::min<int64_t>(nchunk, wave);
   KVC_CHECK_ARG(nchunk <= 65535, KVC_EINVAL);
-  const dim3 grid((a.cols + kCalibThreads - 1) / kCalibThreads, (unsigned)nchunk);
+  const dim3 grid(gx, (unsigned)nchunk);
   cudaStream_t st = (cudaStream_t)stream;
-#define KVC_CALIB(VV, EE) calib_partial_kernel<VV, EE><<<grid, kCalibThreads, 0, st>>>(a)
+#define KVC_CALIB(VV, EE) calib_partial_kernel<VV, EE><<<grid, threads, 0, st>>>(a)
   if (dtype == KVC_BF16) {
     if (V == 8) KVC_CALIB(8, Bf16); else if (V == 2) KVC_CALIB(2, Bf16); else KVC_CALIB(1, Bf16);
   } else {
@@ -179,7 +233,7 @@ extern "C" int kvc_calibration_accumulate(const void* q, int dtype, int64_t n_to
   int rc = launch_status();
   if (rc != KVC_OK) return rc;
   const int64_t total = 3LL * heads * F + (int64_t)heads * P;
-  calib_finalize_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
+  calib_finalize_kernel<<<(unsigned)((total * 32 + 255) / 256), 256, 0, st>>>(
       workspace, nchunk, a.cols, a.rope_cols, heads, F, P, V, re_sum, im_sum, abs_sum, pass_sum);
   return launch_status();
 }

@@ -202,7 +202,7 @@ __device__ __forceinline__ void page_epilogue(const ScoreArgs& a, float (&acc)[k
   const int heads = a.kvh * G;
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    float* row = a.raw + ((int64_t)(l * a.kvh + h) * G + g) * a.tok_total + (int64_t)p * kBlock;
+    float* row = a.raw + (((int64_t)l * a.total_pages + p) * heads + h * G + g) * kBlock;
     float s = 0.f;
 #pragma unroll
     for (int i = 0; i < kTokPerLane; ++i) {
@@ -422,51 +422,72 @@ __global__ void __launch_bounds__(256) head_stats_kernel(const float* __restrict
 // normalisation, head max, layer aggregation
 // --------------------------------------------------------------------------
 
+// a / b from the correctly rounded reciprocal rcp = RN(1/b): q0 = RN(a * rcp),
+// residual r = a - q0 * b (exact by FMA), q = RN(q0 + r * rcp).  Markstein's
+// correction step (P. Markstein, "Computation of elementary functions on the
+// IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990) returns the
+// correctly rounded quotient for normal operands, as IEEE division would; the
+// denominators here are >= 1e-3 and the numerators finite or NaN/inf, which
+// propagate the same way.  Falls back to the division when a, b are not finite.
+__device__ __forceinline__ float div_by(float a, float b, float rcp) {
+  if (!isfinite(a) || !isfinite(b)) return __fdiv_rn(a, b);
+  const float q0 = __fmul_rn(a, rcp);
+  const float r = __fmaf_rn(-q0, b, a);
+  return __fmaf_rn(r, rcp, q0);
+}
+
+// Grid (token blocks, scoring layers): one thread per (token, layer).  A CTA
+// covers 256 tokens = two pages, hence at most two requests; their per-head
+// mean and denominator for this layer are staged in shared memory.  The
+// thread writes the layer's head-max row; aggregate_rows then reduces the
+// layers (the same path serves TP=1 and the TP all-reduce).
 __global__ void __launch_bounds__(256) normalize_kernel(const float* __restrict__ raw, int L, int heads,
                                                         int64_t tok_total, const float* __restrict__ mean,
                                                         const float* __restrict__ den,
                                                         const int32_t* __restrict__ tokens,
                                                         const int32_t* __restrict__ page_off, int R,
-                                                        int layer_agg, float* rows, float* agg) {
-  const int64_t tok = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+                                                        float* rows) {
+  extern __shared__ float st[];  // [2 requests][heads] mean, den, 1/den
+  const int l = blockIdx.y;
+  const int64_t first = (int64_t)blockIdx.x * blockDim.x;
+  const int r_lo = request_of_page(page_off, R, (int)(first >> 7));
+  const int64_t last = min64(first + blockDim.x, tok_total) - 1;
+  const int r_hi = request_of_page(page_off, R, (int)(last >> 7));
+  for (int i = threadIdx.x; i < 2 * heads; i += blockDim.x) {
+    const int rr = i < heads ? r_lo : r_hi;
+    const int64_t g = ((int64_t)l * R + rr) * heads + i % heads;
+    st[i] = __ldg(mean + g);
+    const float d = __ldg(den + g);
+    st[2 * heads + i] = d;
+    st[4 * heads + i] = __frcp_rn(d);
+  }
+  __syncthreads();
+  const int64_t tok = first + threadIdx.x;
   if (tok >= tok_total) return;
   const int p = (int)(tok >> 7);
   const int r = request_of_page(page_off, R, p);
   const int t = (int)(tok - (int64_t)__ldg(page_off + r) * kBlock);
+  float* out = rows + (int64_t)l * tok_total + tok;
   if (t >= __ldg(tokens + r)) {  // page padding: keep rows finite for the MAX all-reduce
-    if (rows)
-      for (int l = 0; l < L; ++l) rows[(int64_t)l * tok_total + tok] = 0.f;
-    else
-      agg[tok] = 0.f;
+    *out = 0.f;
     return;
   }
-  float acc = 0.f;
-  constexpr int U = 8;  // independent loads in flight per thread
-  for (int l = 0; l < L; ++l) {
-    const float* rl = raw + (int64_t)l * heads * tok_total + tok;
-    const float* mu = mean + ((int64_t)l * R + r) * heads;
-    const float* dn = den + ((int64_t)l * R + r) * heads;
-    float z = -INFINITY;
-    for (int h0 = 0; h0 < heads; h0 += U) {
-      float x[U];
+  const float* mu = st + (r == r_lo ? 0 : heads);
+  const float* dn = st + 2 * heads + (r == r_lo ? 0 : heads);
+  const float* rc = st + 4 * heads + (r == r_lo ? 0 : heads);
+  // page-major raw scores: the page's heads x 128 block is contiguous
+  const float* rl = raw + ((int64_t)l * (tok_total >> 7) + p) * heads * kBlock + (tok & (kBlock - 1));
+  constexpr int U = 16;  // independent loads in flight per thread
+  float z = -INFINITY;
+  for (int h0 = 0; h0 < heads; h0 += U) {
+    float x[U];
 #pragma unroll
-      for (int k = 0; k < U; ++k) x[k] = h0 + k < heads ? __ldg(rl + (int64_t)(h0 + k) * tok_total) : 0.f;
+    for (int k = 0; k < U; ++k) x[k] = h0 + k < heads ? __ldg(rl + (int64_t)(h0 + k) * kBlock) : 0.f;
 #pragma unroll
-      for (int k = 0; k < U; ++k)
-        if (h0 + k < heads) z = nan_max(z, __fdiv_rn(x[k] - __ldg(mu + h0 + k), __ldg(dn + h0 + k)));
-    }
-    if (rows) {
-      rows[(int64_t)l * tok_total + tok] = z;
-    } else if (l == 0) {
-      acc = z;
-    } else {
-      acc = layer_agg == KVC_AGG_MEAN ? acc + z : nan_max(acc, z);
-    }
+    for (int k = 0; k < U; ++k)
+      if (h0 + k < heads) z = nan_max(z, div_by(x[k] - mu[h0 + k], dn[h0 + k], rc[h0 + k]));
   }
-  if (!rows) {
-    if (layer_agg == KVC_AGG_MEAN) acc = __fdiv_rn(acc, (float)L);
-    agg[tok] = finalize_score(acc);
-  }
+  *out = z;
 }
 
 __global__ void __launch_bounds__(256) aggregate_rows_kernel(const float* __restrict__ rows, int L,
@@ -639,16 +660,19 @@ extern "C" int kvc_normalize_aggregate(const float* raw, int L, int heads, int t
                                        const float* denom, const int32_t* tokens, const int32_t* page_off,
                                        int R, int layer_aggregation, float* rows_out, float* agg_out,
                                        void* stream) {
-  KVC_CHECK_ARG(raw && mean && denom && tokens && page_off, KVC_ENULL);
-  KVC_CHECK_ARG(rows_out || agg_out, KVC_ENULL);
-  KVC_CHECK_ARG(L > 0 && heads > 0 && R >= 0 && total_pages >= 0, KVC_EINVAL);
+  KVC_CHECK_ARG(raw && mean && denom && tokens && page_off && rows_out, KVC_ENULL);
+  KVC_CHECK_ARG(L > 0 && L <= 65535 && heads > 0 && R >= 0 && total_pages >= 0, KVC_EINVAL);
   KVC_CHECK_ARG(layer_aggregation == KVC_AGG_MEAN || layer_aggregation == KVC_AGG_MAX, KVC_EINVAL);
   if (R == 0 || total_pages == 0) return KVC_OK;
   const int64_t tok_total = (int64_t)total_pages * kBlock;
-  const unsigned grid = (unsigned)((tok_total + 255) / 256);
-  normalize_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(raw, L, heads, tok_total, mean, denom, tokens,
-                                                           page_off, R, layer_aggregation, rows_out, agg_out);
-  return launch_status();
+  const dim3 grid((unsigned)((tok_total + 255) / 256), (unsigned)L);
+  const size_t smem = (size_t)6 * heads * sizeof(float);
+  if (smem > 48 * 1024) return KVC_EUNSUPPORTED;
+  cudaStream_t st = (cudaStream_t)stream;
+  normalize_kernel<<<grid, 256, smem, st>>>(raw, L, heads, tok_total, mean, denom, tokens, page_off, R, rows_out);
+  const int rc = launch_status();
+  if (rc != KVC_OK || agg_out == nullptr) return rc;
+  return kvc_aggregate_rows(rows_out, L, total_pages, tokens, page_off, R, layer_aggregation, agg_out, stream);
 }
 
 extern "C" int kvc_aggregate_rows(const float* rows, int L, int total_pages, const int32_t* tokens,

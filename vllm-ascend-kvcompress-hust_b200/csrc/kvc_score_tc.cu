@@ -93,11 +93,10 @@ __global__ void __launch_bounds__(256) prepare_frag_kernel(const __grid_constant
   __syncthreads();
   const int S = frag_steps(a.F, a.P);
   const int kf = a.F / 16;
-  const int64_t total = (int64_t)a.kvh * S * 32;
-  for (int64_t i = threadIdx.x; i < total; i += blockDim.x) {
+  const int h = blockIdx.z;
+  for (int i = threadIdx.x; i < S * 32; i += blockDim.x) {
     const int lane = i % 32;
-    const int s = (i / 32) % S;
-    const int h = i / (32 * S);
+    const int s = i / 32;
     uint32_t words[4];
     for (int t = 0; t < 2; ++t) {          // n-tile: 0 = hi columns, 1 = lo columns
       const int g = lane / 4;              // column within the n-tile = query head
@@ -495,7 +494,7 @@ __global__ void __launch_bounds__(kTcThreads, TcGeom<F, P>::kMinBlocks) score_tc
 #pragma unroll
       for (int o = 4; o < 32; o <<= 1) m2 += __shfl_xor_sync(0xffffffffu, m2, o);
       if (g < a.G) {
-        float* row = a.raw + ((int64_t)mu.lg * heads + mu.h * a.G + g) * a.tok_total + (int64_t)mu.p * kBlock;
+        float* row = a.raw + (((int64_t)mu.lg * a.total_pages + mu.p) * heads + mu.h * a.G + g) * kBlock;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int t = warp * 32 + (i >> 1) * 16 + (i & 1) * 8 + (lane >> 2);
@@ -619,7 +618,7 @@ extern "C" int kvc_prepare_score_fragments(const float* omega, const float* offs
   if (R == 0) return KVC_OK;
   FragArgs a{omega, offsets, round_start, q_real, q_imag, scale, extra, q_pass, frag_out,
              n_off, R, L, kvh, G, F, P, dtype == KVC_FP16 ? 1 : 0};
-  prepare_frag_kernel<<<dim3(L, R), 256, 2 * F * sizeof(float), (cudaStream_t)stream>>>(a);
+  prepare_frag_kernel<<<dim3(L, R, kvh), 256, 2 * F * sizeof(float), (cudaStream_t)stream>>>(a);
   return launch_status();
 }
 

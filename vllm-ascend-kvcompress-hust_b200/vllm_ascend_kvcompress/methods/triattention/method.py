@@ -408,15 +408,16 @@ class TriAttentionMethod(KVCompressionMethod):
         self._mark("head_stats")
         K.head_stats(partial, L, heads, plan, mean, var, den, parts)
         self._mark("normalize")
+        rows = ws.get("rows", L * tok, torch.float32)
         if self.tensor_parallel_size > 1:
-            rows = ws.get("rows", L * tok, torch.float32)
             K.normalize_aggregate(raw, L, heads, plan, mean, den, self.layer_aggregation_code, rows_out=rows)
             self._mark("tp_sync")
             self._tp_all_reduce_max(rows)
             self._mark("aggregate_rows")
             K.aggregate_rows(rows, L, plan, self.layer_aggregation_code, agg)
         else:
-            K.normalize_aggregate(raw, L, heads, plan, mean, den, self.layer_aggregation_code, agg_out=agg)
+            K.normalize_aggregate(raw, L, heads, plan, mean, den, self.layer_aggregation_code, rows_out=rows,
+                                  agg_out=agg)
         self._mark("select")
         policy = N.POLICY_V3 if cfg.position_policy == "v3" else N.POLICY_GLOBAL
         K.select_keep(agg, plan, cfg.kv_budget, cfg.protected_prefix_window, cfg.protected_recent_window,
