@@ -118,7 +118,8 @@ int kvc_score_paged_keys(const void* const* k_layers, int num_layers, int dtype,
  *   key_maps     host array of num_layers 128-byte TMA descriptors from
  *                kvc_encode_key_maps (built once per cache binding).
  *   frag         kvc_prepare_score_fragments output.
- *   partial_out  [L][total_pages*4][kvh*G][2]: moments per quarter page.
+ *   partial_out  [L][total_pages*4][kvh*G][2]: (sum, sum of squared
+ *                deviations from the partial's mean) per quarter page.
  */
 int kvc_tc_supported(int group, int head_dim, int rotary_dim);
 int kvc_encode_key_maps(const void* const* k_layers, int num_layers, int dtype, int64_t block_stride,

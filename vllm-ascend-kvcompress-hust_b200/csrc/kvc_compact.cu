@@ -27,7 +27,7 @@ struct CompactArgs {
   const int64_t* keep;
   const int32_t* tokens;
   int32_t* error_flag;
-  int N, R, budget;
+  int N, R, budget, tile_rows;
 };
 
 template <int VEC>
@@ -76,16 +76,17 @@ __global__ void __launch_bounds__(kCopyThreads) compact_kernel(const __grid_cons
   using T = typename Vec<VEC>::T;
   const int lane = threadIdx.x & 31;
   const int64_t rows = (int64_t)a.N * 2 * a.R * a.budget;
-  const int64_t tiles = (rows + 31) / 32;
+  const int tr = a.tile_rows;  // rows per warp tile (<= 32; fewer for small problems)
+  const int64_t tiles = (rows + tr - 1) / tr;
   const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int nvec = (int)(a.row_bytes / VEC);
   for (int64_t tile = warp0; tile < tiles; tile += nwarps) {
-    const int64_t q = tile * 32 + lane;
+    const int64_t q = tile * tr + lane;
     const char* my_src = nullptr;
     char* my_dst = nullptr;
-    if (q < rows) resolve_row(a, q, my_src, my_dst);
-    const int nrows = (int)min64(32, rows - tile * 32);
+    if (lane < tr && q < rows) resolve_row(a, q, my_src, my_dst);
+    const int nrows = (int)min64(tr, rows - tile * tr);
     for (int k = 0; k < nrows; k += 2) {
       const char* s0 = (const char*)__shfl_sync(0xffffffffu, (unsigned long long)my_src, k);
       char* d0 = (char*)__shfl_sync(0xffffffffu, (unsigned long long)my_dst, k);
@@ -232,7 +233,10 @@ extern "C" int kvc_compact(const void* const* k_layers, const void* const* v_lay
     a.R = R;
     a.budget = budget;
     const int64_t rows = (int64_t)a.N * 2 * R * budget;
-    const unsigned grid = copy_grid((rows + 31) / 32);
+    // enough warps to fill the GPU: shrink the per-warp tile when rows are few
+    const int64_t full = (int64_t)sm_count() * (2048 / 32);
+    a.tile_rows = (int)std::max<int64_t>(1, std::min<int64_t>(32, rows / full));
+    const unsigned grid = copy_grid((rows + a.tile_rows - 1) / a.tile_rows);
     switch (vec) {
       case 16: compact_kernel<16><<<grid, kCopyThreads, 0, st>>>(a); break;
       case 8: compact_kernel<8><<<grid, kCopyThreads, 0, st>>>(a); break;

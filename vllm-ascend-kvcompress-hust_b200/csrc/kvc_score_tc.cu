@@ -72,19 +72,35 @@ __device__ __forceinline__ float from_half_bits(uint16_t v, int fp16) {
 
 __global__ void __launch_bounds__(256) prepare_frag_kernel(const __grid_constant__ FragArgs a) {
   extern __shared__ float sm[];
-  float* cm = sm;          // [F] mean cos
-  float* sn = sm + a.F;    // [F] mean sin
-  const int l = blockIdx.x, r = blockIdx.y;
+  float* cm = sm;                      // [F] mean cos
+  float* sn = sm + a.F;                // [F] mean sin
+  float* tc = sm + 2 * a.F;            // [n_off][F] cos
+  float* ts = tc + a.n_off * a.F;      // [n_off][F] sin
+  float* qs = ts + a.n_off * a.F;      // [4][G][F] q_real, q_imag, scale, extra of this (layer, head)
+  const int l = blockIdx.x, r = blockIdx.y, h = blockIdx.z;
   const float rs = (float)a.round_start[r];
+  {
+    const int gf = a.G * a.F;
+    const int64_t base = (int64_t)(l * a.kvh + h) * gf;
+    for (int i = threadIdx.x; i < gf; i += blockDim.x) {
+      qs[i] = a.q_real[base + i];
+      qs[gf + i] = a.q_imag[base + i];
+      qs[2 * gf + i] = a.scale[base + i];
+      qs[3 * gf + i] = a.extra[base + i];
+    }
+  }
+  for (int i = threadIdx.x; i < a.n_off * a.F; i += blockDim.x) {
+    const int o = i / a.F, f = i % a.F;
+    // fp32 (offset + round_start) then * omega, as the reference forms phases
+    const float ph = __fmul_rn(__fadd_rn(a.offsets[o], rs), a.omega[l * a.F + f]);
+    sincosf(ph, &ts[i], &tc[i]);
+  }
+  __syncthreads();
   for (int f = threadIdx.x; f < a.F; f += blockDim.x) {
-    const float w = a.omega[l * a.F + f];
     float cs = 0.f, ss = 0.f;
-    for (int o = 0; o < a.n_off; ++o) {
-      const float ph = __fmul_rn(__fadd_rn(a.offsets[o], rs), w);
-      float s, c;
-      sincosf(ph, &s, &c);
-      cs += c;
-      ss += s;
+    for (int o = 0; o < a.n_off; ++o) {  // offsets summed in order
+      cs += tc[o * a.F + f];
+      ss += ts[o * a.F + f];
     }
     const float inv = 1.0f / (float)a.n_off;
     cm[f] = cs * inv;
@@ -93,7 +109,7 @@ __global__ void __launch_bounds__(256) prepare_frag_kernel(const __grid_constant
   __syncthreads();
   const int S = frag_steps(a.F, a.P);
   const int kf = a.F / 16;
-  const int h = blockIdx.z;
+  const int gf = a.G * a.F;
   for (int i = threadIdx.x; i < S * 32; i += blockDim.x) {
     const int lane = i % 32;
     const int s = i / 32;
@@ -110,11 +126,11 @@ __global__ void __launch_bounds__(256) prepare_frag_kernel(const __grid_constant
             const int part = s < kf ? 0 : s < 2 * kf ? 1 : s < 3 * kf ? 2 : s < 4 * kf ? 3 : 4;
             if (part < 4) {
               const int f = (s - part * kf) * 16 + k;
-              const int64_t src = ((int64_t)(l * a.kvh + h) * a.G + g) * a.F + f;
-              const float qr = a.q_real[src], qi = a.q_imag[src], sc = a.scale[src];
+              const int src = g * a.F + f;
+              const float qr = qs[src], qi = qs[gf + src], sc = qs[2 * gf + src];
               if (part == 0) v = sc * (qr * cm[f] - qi * sn[f]);
               else if (part == 1) v = sc * (qi * cm[f] + qr * sn[f]);
-              else v = a.extra[src] * sc;
+              else v = qs[3 * gf + src] * sc;
               lo_zero = part == 3;  // m_lo rows pair with e_hi only
             } else {
               const int p = (s - 4 * kf) * 16 + k;
@@ -222,7 +238,7 @@ __device__ __forceinline__ void mma16816<Fp16>(float (&d)[4], const uint32_t (&a
 
 __device__ __forceinline__ float sqrt_approx(float x) {
   float y;
-  asm("sqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
@@ -618,7 +634,9 @@ extern "C" int kvc_prepare_score_fragments(const float* omega, const float* offs
   if (R == 0) return KVC_OK;
   FragArgs a{omega, offsets, round_start, q_real, q_imag, scale, extra, q_pass, frag_out,
              n_off, R, L, kvh, G, F, P, dtype == KVC_FP16 ? 1 : 0};
-  prepare_frag_kernel<<<dim3(L, R, kvh), 256, 2 * F * sizeof(float), (cudaStream_t)stream>>>(a);
+  const size_t smem = ((size_t)(2 + 2 * n_off) * F + (size_t)4 * G * F) * sizeof(float);
+  KVC_CHECK_ARG(smem <= 48 * 1024, KVC_EUNSUPPORTED);
+  prepare_frag_kernel<<<dim3(L, R, kvh), 256, smem, (cudaStream_t)stream>>>(a);
   return launch_status();
 }
 
