@@ -187,6 +187,10 @@ EDGE_CASES = {
     "g2_d64": _edge("g2_d64", W.Geometry(2, 2, 4, 64, 64, 1e4),
                     W.Options(kv_budget=384, protected_prefix_window=8, protected_recent_window=64,
                               position_segments=3, score_layer_stride=1), [1000, 385, 4000], 25),
+    # three KV heads of 64 dims: 384-byte rows, not a power-of-two count of vectors
+    "kvh3_d64": _edge("kvh3_d64", W.Geometry(2, 3, 6, 64, 64, 1e4),
+                      W.Options(kv_budget=512, protected_prefix_window=16, protected_recent_window=64,
+                                score_layer_stride=1), [1500, 700, 2600], 27),
     # a ragged batch of many requests
     "ragged": _edge("ragged", W.Geometry(2, 8, 40, 128, 128, 1e6),
                     W.Options(kv_budget=640, protected_prefix_window=64, protected_recent_window=128,

@@ -6,7 +6,9 @@
 // source/destination addresses (keep index -> source block -> address, with
 // range checks) so the dependent index loads of 32 rows overlap; the warp then
 // streams the rows with 16-byte vectors (narrower when the caller's strides or
-// bases are not 16-byte aligned), two rows in flight per pass.
+// bases are not 16-byte aligned), two rows in flight per pass.  Rows under
+// 2 KB (few local heads under tensor parallelism) are copied as one flat
+// (row, vector) range per tile so each lane still has eight vectors in flight.
 #include "kvc_common.cuh"
 
 namespace kvc {
@@ -28,6 +30,7 @@ struct CompactArgs {
   const int32_t* tokens;
   int32_t* error_flag;
   int N, R, budget, tile_rows;
+  int nvec_shift;  // log2(row_bytes / vector width) when a power of two, else -1
 };
 
 template <int VEC>
@@ -71,8 +74,8 @@ __device__ __forceinline__ void resolve_row(const CompactArgs& a, int64_t q, con
   dst = base_d + db * a.block_stride + (j & 127) * a.row_bytes;
 }
 
-template <int VEC>
-__global__ void __launch_bounds__(kCopyThreads) compact_kernel(const __grid_constant__ CompactArgs a) {
+template <int VEC, bool SMALL>
+__global__ void __launch_bounds__(kCopyThreads, SMALL ? 3 : 4) compact_kernel(const __grid_constant__ CompactArgs a) {
   using T = typename Vec<VEC>::T;
   const int lane = threadIdx.x & 31;
   const int64_t rows = (int64_t)a.N * 2 * a.R * a.budget;
@@ -87,6 +90,32 @@ __global__ void __launch_bounds__(kCopyThreads) compact_kernel(const __grid_cons
     char* my_dst = nullptr;
     if (lane < tr && q < rows) resolve_row(a, q, my_src, my_dst);
     const int nrows = (int)min64(tr, rows - tile * tr);
+    if constexpr (SMALL) {
+      // rows narrower than 2 KB: spread the tile's (row, vector) pairs over the
+      // lanes so that every lane keeps kSmallU vectors in flight
+      constexpr int kSmallU = 8;
+      const int total = nrows * nvec;
+      for (int e0 = 0; e0 < total; e0 += 32 * kSmallU) {
+        T x[kSmallU];
+        char* dd[kSmallU];
+#pragma unroll
+        for (int u = 0; u < kSmallU; ++u) {
+          const int e = e0 + u * 32 + lane;
+          const int row = min(a.nvec_shift >= 0 ? e >> a.nvec_shift : e / nvec, nrows - 1);
+          const char* s = (const char*)__shfl_sync(0xffffffffu, (unsigned long long)my_src, row);
+          char* d = (char*)__shfl_sync(0xffffffffu, (unsigned long long)my_dst, row);
+          dd[u] = nullptr;
+          if (e < total && s) {
+            const int64_t off = (int64_t)(e - row * nvec) * VEC;
+            x[u] = load_nc<VEC>(s + off);
+            dd[u] = d + off;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kSmallU; ++u)
+          if (dd[u]) *reinterpret_cast<T*>(dd[u]) = x[u];
+      }
+    } else {
     for (int k = 0; k < nrows; k += 2) {
       const char* s0 = (const char*)__shfl_sync(0xffffffffu, (unsigned long long)my_src, k);
       char* d0 = (char*)__shfl_sync(0xffffffffu, (unsigned long long)my_dst, k);
@@ -113,6 +142,7 @@ __global__ void __launch_bounds__(kCopyThreads) compact_kernel(const __grid_cons
           }
         }
       }
+    }
     }
   }
 }
@@ -183,10 +213,30 @@ inline int vec_width(uintptr_t bits) {
   return 0;
 }
 
-inline unsigned copy_grid(int64_t work_warps) {
-  const int64_t cap = (int64_t)sm_count() * (2048 / kCopyThreads);
+inline unsigned copy_grid(int64_t work_warps, int blocks_per_sm = 2048 / kCopyThreads) {
+  const int64_t cap = (int64_t)sm_count() * blocks_per_sm;
   const int64_t want = (work_warps * 32 + kCopyThreads - 1) / kCopyThreads;
   return (unsigned)std::max<int64_t>(1, std::min(cap, want));
+}
+
+// Resident CTAs per SM of one compaction variant (register-limited), so the
+// grid-stride loop runs as a single wave.
+template <int VEC, bool SMALL>
+int compact_blocks_per_sm() {
+  static int n = 0;
+  if (n == 0) {
+    int b = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, compact_kernel<VEC, SMALL>, kCopyThreads, 0) != cudaSuccess ||
+        b <= 0)
+      b = 2048 / kCopyThreads;
+    n = b;
+  }
+  return n;
+}
+
+template <int VEC, bool SMALL>
+void launch_compact(const CompactArgs& a, int64_t tiles, cudaStream_t st) {
+  compact_kernel<VEC, SMALL><<<copy_grid(tiles, compact_blocks_per_sm<VEC, SMALL>()), kCopyThreads, 0, st>>>(a);
 }
 
 }  // namespace kvc
@@ -236,12 +286,23 @@ extern "C" int kvc_compact(const void* const* k_layers, const void* const* v_lay
     // enough warps to fill the GPU: shrink the per-warp tile when rows are few
     const int64_t full = (int64_t)sm_count() * (2048 / 32);
     a.tile_rows = (int)std::max<int64_t>(1, std::min<int64_t>(32, rows / full));
-    const unsigned grid = copy_grid((rows + a.tile_rows - 1) / a.tile_rows);
-    switch (vec) {
-      case 16: compact_kernel<16><<<grid, kCopyThreads, 0, st>>>(a); break;
-      case 8: compact_kernel<8><<<grid, kCopyThreads, 0, st>>>(a); break;
-      case 4: compact_kernel<4><<<grid, kCopyThreads, 0, st>>>(a); break;
-      default: compact_kernel<2><<<grid, kCopyThreads, 0, st>>>(a); break;
+    const int64_t nvec = row_bytes / vec;
+    a.nvec_shift = (nvec & (nvec - 1)) == 0 ? __builtin_ctzll((unsigned long long)nvec) : -1;
+    const int64_t tiles = (rows + a.tile_rows - 1) / a.tile_rows;
+    if (nvec < 128) {
+      switch (vec) {
+        case 16: launch_compact<16, true>(a, tiles, st); break;
+        case 8: launch_compact<8, true>(a, tiles, st); break;
+        case 4: launch_compact<4, true>(a, tiles, st); break;
+        default: launch_compact<2, true>(a, tiles, st); break;
+      }
+    } else {
+      switch (vec) {
+        case 16: launch_compact<16, false>(a, tiles, st); break;
+        case 8: launch_compact<8, false>(a, tiles, st); break;
+        case 4: launch_compact<4, false>(a, tiles, st); break;
+        default: launch_compact<2, false>(a, tiles, st); break;
+      }
     }
     const int rc = launch_status();
     if (rc != KVC_OK) return rc;

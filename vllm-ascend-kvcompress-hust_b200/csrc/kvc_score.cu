@@ -465,7 +465,7 @@ __global__ void __launch_bounds__(256) normalize_kernel(const float* __restrict_
   const int64_t tok = first + threadIdx.x;
   if (tok >= tok_total) return;
   const int p = (int)(tok >> 7);
-  const int r = request_of_page(page_off, R, p);
+  const int r = p == (int)(first >> 7) ? r_lo : r_hi;  // a 256-token block spans two pages
   const int t = (int)(tok - (int64_t)__ldg(page_off + r) * kBlock);
   float* out = rows + (int64_t)l * tok_total + tok;
   if (t >= __ldg(tokens + r)) {  // page padding: keep rows finite for the MAX all-reduce
@@ -495,10 +495,13 @@ __global__ void __launch_bounds__(256) aggregate_rows_kernel(const float* __rest
                                                              const int32_t* __restrict__ tokens,
                                                              const int32_t* __restrict__ page_off, int R,
                                                              int layer_agg, float* agg) {
-  const int64_t tok = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t first = (int64_t)blockIdx.x * blockDim.x;  // 256 tokens: two pages
+  const int r_lo = request_of_page(page_off, R, (int)(first >> 7));
+  const int r_hi = request_of_page(page_off, R, (int)((min64(first + blockDim.x, tok_total) - 1) >> 7));
+  const int64_t tok = first + threadIdx.x;
   if (tok >= tok_total) return;
   const int p = (int)(tok >> 7);
-  const int r = request_of_page(page_off, R, p);
+  const int r = p == (int)(first >> 7) ? r_lo : r_hi;
   const int t = (int)(tok - (int64_t)__ldg(page_off + r) * kBlock);
   if (t >= __ldg(tokens + r)) {
     agg[tok] = 0.f;
