@@ -267,6 +267,111 @@ int kvc_shift_positions(const int64_t* positions, const void* request_indices, i
                         const int64_t* offsets, int64_t num_offsets, int64_t n, int64_t* out,
                         int32_t* error_flag, void* stream);
 
+/*
+ * One compression step in a single call.
+ *
+ * No reference counterpart: the reference issues each device op from Python
+ * (TriAttentionMethod._select_keep_indices and compress,
+ * methods/triattention/method.py:256-475).  The descriptor holds what the
+ * entry points above take; the fields under "bound once" are filled when the
+ * method binds the KV cache, the rest before each step.  kvc_triattention_run
+ * validates and launches the selected stages in order on `stream`, exactly as
+ * the individual entry points would, so a step costs one host call instead of
+ * seven.  Stages:
+ *   KVC_STAGE_TABLES    gather the per-request block tables (src_tables /
+ *                       dst_tables: device arrays of device pointers) into
+ *                       the CSR arrays src_blocks / dst_blocks
+ *   KVC_STAGE_SCORE     prepare fragments/coefficients, score, head stats and
+ *                       normalise into rows (kvc_prepare_score_fragments +
+ *                       kvc_score_paged_keys_tc, or the FMA pair; kvc_head_stats;
+ *                       kvc_normalize_aggregate)
+ *   KVC_STAGE_AGGREGATE layer reduction into agg (kvc_aggregate_rows)
+ *   KVC_STAGE_SELECT    kvc_select_keep into keep
+ *   KVC_STAGE_COMPACT   kvc_compact (+ commit staging when staged_rows/offsets)
+ * A tensor-parallel caller runs TABLES | SCORE, all-reduces rows with MAX, then
+ * runs AGGREGATE | SELECT | COMPACT.  stage_events (optional: KVC_STEP_EVENTS
+ * cudaEvent_t handles, NULL entries skipped) are recorded on `stream` before
+ * the prepare, score, head-stats, normalise, aggregate, select and compact
+ * launches of the stages that run, and after the last launch, for per-stage
+ * timing.  Returns the first non-zero status; later stages are not launched.
+ */
+#define KVC_SCORER_TENSOR 0     /* kvc_score_paged_keys_tc (needs key_maps) */
+#define KVC_SCORER_FMA 1        /* kvc_score_paged_keys (needs score_k) */
+#define KVC_STAGE_SCORE 1
+#define KVC_STAGE_AGGREGATE 2
+#define KVC_STAGE_SELECT 4
+#define KVC_STAGE_COMPACT 8
+#define KVC_STAGE_TABLES 16
+#define KVC_STAGE_ALL 31
+#define KVC_STEP_EVENTS 8
+
+typedef struct kvc_triattention_step {
+  /* bound once */
+  int32_t scorer;              /* KVC_SCORER_* */
+  int32_t kv_dtype;            /* KVC_BF16 / KVC_FP16 */
+  int32_t score_layers;        /* L_s */
+  int32_t kv_heads;            /* local KV heads */
+  int32_t group;               /* query heads per KV head */
+  int32_t head_dim;
+  int32_t rotary_dim;
+  int32_t n_off;               /* geometric offsets */
+  int32_t score_aggregation;   /* KVC_AGG_* over offsets (FMA scorer) */
+  int32_t layer_aggregation;   /* KVC_AGG_* over layers */
+  int32_t budget;
+  int32_t prefix;
+  int32_t recent;
+  int32_t segments;
+  int32_t policy;              /* KVC_POLICY_* */
+  int32_t compact_layers;      /* N, every materialised layer */
+  int64_t num_blocks;
+  int64_t block_stride;        /* elements between blocks (FMA scorer) */
+  int64_t block_stride_bytes;
+  int64_t row_bytes;           /* kv_heads * head_dim * element size */
+  const void* key_maps;        /* [L_s] TMA descriptors (tensor scorer) */
+  const void* const* score_k;  /* [L_s] K caches of the scoring layers (FMA scorer) */
+  const void* const* k_layers; /* [N] */
+  const void* const* v_layers; /* [N] */
+  const float* omega;          /* [L_s][F] */
+  const float* offsets;        /* [n_off] */
+  const float* q_real;         /* [L_s][kvh][G][F] */
+  const float* q_imag;
+  const float* scale;
+  const float* extra;
+  const float* q_pass;         /* [L_s][kvh][G][P] or NULL (tensor scorer) */
+  const float* q_pass_t;       /* [L_s][kvh][P][G] or NULL (FMA scorer) */
+  /* per step */
+  int32_t num_requests;
+  int32_t total_pages;
+  const int32_t* tokens;
+  const int32_t* page_off;
+  int64_t* src_blocks;         /* CSR by src_block_off; written by KVC_STAGE_TABLES */
+  const int64_t* src_block_off;
+  int64_t* dst_blocks;         /* CSR by dst_block_off; written by KVC_STAGE_TABLES */
+  const int64_t* dst_block_off;
+  const int64_t* round_start;
+  const int64_t* semantic;
+  const int64_t* const* src_tables; /* [R] per-request source tables (KVC_STAGE_TABLES) */
+  const int64_t* const* dst_tables; /* [R] destination tables, or NULL */
+  /* caller-owned workspaces, sized as for the individual entry points */
+  void* score_coef;            /* fragments (tensor) or coefficients (FMA) */
+  float* raw;
+  float* partial;
+  float* mean;
+  float* var;
+  float* den;
+  float* rows;
+  float* agg;
+  int64_t* keep;
+  int64_t* staged_rows;        /* optional commit staging */
+  int32_t staged_row_stride;
+  int64_t* staged_offsets;
+  int32_t* error_flag;
+} kvc_triattention_step;
+
+int64_t kvc_triattention_step_size(void);   /* sizeof(kvc_triattention_step), for bindings */
+int kvc_triattention_run(const kvc_triattention_step* step, int stages, void* const* stage_events,
+                         void* stream);
+
 #ifdef __cplusplus
 }
 #endif

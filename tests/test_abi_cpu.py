@@ -99,3 +99,26 @@ def test_kernels_refuse_cpu_tensors():
                             policy="v3")
     with pytest.raises(RuntimeError, match="CUDA"):
         K.require_cuda(torch.zeros(1))
+
+
+def test_step_descriptor_matches_header_field_for_field():
+    body = re.search(r"typedef struct kvc_triattention_step \{(.*?)\} kvc_triattention_step;", HEADER.read_text(),
+                     re.S).group(1)
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    fields = re.findall(r"(\w+)\s*;", body)
+    assert fields == [f for f, _ in N.TriAttentionStep._fields_]
+    assert N.lib().kvc_triattention_step_size() == ctypes.sizeof(N.TriAttentionStep)
+    for name, ctype in N.TriAttentionStep._fields_:
+        decl = re.search(r"([\w\s\*]+?)\b" + name + r"\s*;", body).group(1)
+        assert ("*" in decl) == (ctype is ctypes.c_void_p), name
+        if ctype is not ctypes.c_void_p:
+            assert decl.split()[-1] == {ctypes.c_int32: "int32_t", ctypes.c_int64: "int64_t"}[ctype], name
+
+
+def test_step_rejects_bad_stage_masks_without_launch():
+    lib = N.lib()
+    st = N.TriAttentionStep()
+    assert lib.kvc_triattention_run(None, N.STAGE_ALL, None, None) == -14
+    assert lib.kvc_triattention_run(ctypes.byref(st), 0, None, None) == -22
+    assert lib.kvc_triattention_run(ctypes.byref(st), 32, None, None) == -22
+    assert lib.kvc_triattention_run(ctypes.byref(st), N.STAGE_TABLES, None, None) == -14

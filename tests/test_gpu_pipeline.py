@@ -116,6 +116,87 @@ def test_per_request_compress_equals_batched(tmp_path):
         assert int(m2.staged_offsets[row]) == w.lengths[i] - w.options.kv_budget
 
 
+@pytest.mark.parametrize("scorer", ["tensor", "fma"])
+def test_single_call_step_equals_entry_points_one_by_one(scorer, tmp_path, monkeypatch):
+    """kvc_triattention_run launches exactly what the individual entry points do."""
+    from vllm_ascend_kvcompress import _native as N
+    from vllm_ascend_kvcompress.methods.triattention import kernels as K
+
+    monkeypatch.setenv("KVC_B200_SCORER", scorer)
+    w = W.config0()
+    cpu = cpu_caches(w)
+    g1, g2 = to_gpu(cpu), to_gpu(cpu)
+    m = bind(w, g1, tmp_path)
+    reqs = W.b200_requests(w)
+    m.compress_many(reqs)
+    m.check_device_errors()
+    keep1 = m._ws.get("keep", len(reqs) * w.options.kv_budget, torch.int64).clone()
+    agg1 = m.last_stats[3].clone()
+    # the same step through the per-stage entry points, on a second copy of the caches
+    m2 = bind(w, g2, tmp_path)
+    plan = m2._plan([(r.physical_num_tokens, r.semantic_num_tokens, r.source_block_ids_device,
+                      r.destination_block_ids_device) for r in reqs])
+    m2._gather_tables(plan)
+    L, heads, R, tok = m2.scoring_layer_count, m2.local_kv_heads * m2.group, plan.num_requests, plan.tok_total
+    parts = 4 if m2.use_tensor_scorer else 1
+    f32 = lambda n: torch.empty(n, dtype=torch.float32, device="cuda")
+    raw, partial = f32(L * heads * tok), f32(L * plan.total_pages * parts * heads * 2)
+    mean, var, den, rows, agg = f32(L * R * heads), f32(L * R * heads), f32(L * R * heads), f32(L * tok), f32(tok)
+    keep = torch.empty(R * w.options.kv_budget, dtype=torch.int64, device="cuda")
+    if m2.use_tensor_scorer:
+        frag = torch.empty(R * L * m2.local_kv_heads * m2.frag_block, dtype=torch.int32, device="cuda")
+        K.prepare_score_fragments(m2.scoring_omega, m2.offsets, plan, m2.scoring_q_real, m2.scoring_q_imag,
+                                  m2.scoring_scale, m2.scoring_extra, m2.scoring_q_pass, m2.kv_dtype, frag)
+        K.score_paged_keys_tc(m2._key_maps, L, m2.kv_dtype, m2.num_blocks, m2.local_kv_heads, m2.group,
+                              m2.head_dim, m2.rotary_dim, plan, frag, raw, partial, m2._err)
+    else:
+        coef = f32(R * L * m2.local_kv_heads * m2.coef_block)
+        K.prepare_score_coefficients(m2.scoring_omega, m2.offsets, plan, m2.scoring_q_real, m2.scoring_q_imag,
+                                     m2.scoring_scale, m2.scoring_extra, m2.score_aggregation_code, coef)
+        K.score_paged_keys(m2._k_score, m2.kv_dtype, m2.block_stride, m2.num_blocks, m2.local_kv_heads, m2.group,
+                           m2.head_dim, m2.rotary_dim, plan, coef, m2.offsets.numel(), m2.score_aggregation_code,
+                           m2.scoring_q_pass_t, raw, partial, m2._err)
+    K.head_stats(partial, L, heads, plan, mean, var, den, parts)
+    K.normalize_aggregate(raw, L, heads, plan, mean, den, m2.layer_aggregation_code, rows_out=rows, agg_out=agg)
+    cfg = m2.config
+    K.select_keep(agg, plan, cfg.kv_budget, cfg.protected_prefix_window, cfg.protected_recent_window,
+                  cfg.position_segments, N.POLICY_V3, keep, m2._err)
+    K.compact(m2._k_all, m2._v_all, m2.block_stride_bytes, m2.num_blocks, m2.row_bytes, plan, keep,
+              cfg.kv_budget, m2._err, None, None)
+    torch.cuda.synchronize()
+    assert int(m2._err.item()) == 0
+    assert torch.equal(agg.view(torch.int32), agg1.view(torch.int32))
+    assert torch.equal(keep, keep1)
+    for (k1, v1), (k2, v2) in zip(g1, g2):
+        assert torch.equal(k1.view(torch.int16), k2.view(torch.int16))
+        assert torch.equal(v1.view(torch.int16), v2.view(torch.int16))
+
+
+def test_block_tables_of_any_int_dtype_and_padding_give_the_same_step(tmp_path):
+    """Tables longer than needed, int32, or strided views are gathered like exact int64 tables."""
+    from dataclasses import replace
+
+    w = W.config0()
+    cpu = cpu_caches(w)
+    g1, g2 = to_gpu(cpu), to_gpu(cpu)
+    m1, m2 = bind(w, g1, tmp_path), bind(w, g2, tmp_path)
+    reqs = W.b200_requests(w)
+    m1.compress_many(reqs)
+    odd = []
+    for j, r in enumerate(reqs):
+        src = torch.cat([r.source_block_ids_device, torch.full((5,), -7, device="cuda", dtype=torch.int64)])
+        dst = torch.stack([r.destination_block_ids_device, r.destination_block_ids_device], 1)[:, 0]  # strided
+        odd.append(replace(r, source_block_ids_device=src.to(torch.int32) if j % 2 else src,
+                           destination_block_ids_device=dst))
+    m2.compress_many(odd)
+    m1.check_device_errors()
+    m2.check_device_errors()
+    torch.cuda.synchronize()
+    for (k1, v1), (k2, v2) in zip(g1, g2):
+        assert torch.equal(k1.view(torch.int16), k2.view(torch.int16))
+        assert torch.equal(v1.view(torch.int16), v2.view(torch.int16))
+
+
 def test_select_keep_indices_hook_matches_batch(tmp_path):
     w = W.config0()
     gpu = to_gpu(cpu_caches(w))

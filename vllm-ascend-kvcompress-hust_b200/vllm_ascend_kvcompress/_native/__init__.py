@@ -58,7 +58,36 @@ _SIGNATURES = {
     "kvc_shift_positions": (c_int, [_P, _P, c_int, _P, c_int64, c_int64, _P, _P, _P]),
     "kvc_calibration_accumulate_noalloc": (
         c_int, [_P, c_int, c_int64, c_int64, c_int, c_int, c_int, _P, _P, _P, _P, _P]),
+    "kvc_triattention_step_size": (c_int64, []),
+    "kvc_triattention_run": (c_int, [_P, c_int, _P, _P]),
 }
+
+SCORER_TENSOR, SCORER_FMA = 0, 1
+STAGE_SCORE, STAGE_AGGREGATE, STAGE_SELECT, STAGE_COMPACT, STAGE_TABLES, STAGE_ALL = 1, 2, 4, 8, 16, 31
+STEP_EVENTS = 8
+STEP_EVENT_NAMES = ("prepare", "score", "head_stats", "normalize", "aggregate_rows", "select", "compact", "end")
+
+
+class TriAttentionStep(ctypes.Structure):
+    """``kvc_triattention_step`` (include/kvc.h), field for field."""
+
+    _fields_ = [
+        ("scorer", c_int32), ("kv_dtype", c_int32), ("score_layers", c_int32), ("kv_heads", c_int32),
+        ("group", c_int32), ("head_dim", c_int32), ("rotary_dim", c_int32), ("n_off", c_int32),
+        ("score_aggregation", c_int32), ("layer_aggregation", c_int32),
+        ("budget", c_int32), ("prefix", c_int32), ("recent", c_int32), ("segments", c_int32), ("policy", c_int32),
+        ("compact_layers", c_int32),
+        ("num_blocks", c_int64), ("block_stride", c_int64), ("block_stride_bytes", c_int64), ("row_bytes", c_int64),
+        ("key_maps", _P), ("score_k", _P), ("k_layers", _P), ("v_layers", _P),
+        ("omega", _P), ("offsets", _P), ("q_real", _P), ("q_imag", _P), ("scale", _P), ("extra", _P),
+        ("q_pass", _P), ("q_pass_t", _P),
+        ("num_requests", c_int32), ("total_pages", c_int32),
+        ("tokens", _P), ("page_off", _P), ("src_blocks", _P), ("src_block_off", _P), ("dst_blocks", _P),
+        ("dst_block_off", _P), ("round_start", _P), ("semantic", _P), ("src_tables", _P), ("dst_tables", _P),
+        ("score_coef", _P), ("raw", _P), ("partial", _P), ("mean", _P), ("var", _P), ("den", _P), ("rows", _P),
+        ("agg", _P), ("keep", _P), ("staged_rows", _P), ("staged_row_stride", c_int32), ("staged_offsets", _P),
+        ("error_flag", _P),
+    ]
 
 _lib: ctypes.CDLL | None = None
 

@@ -38,7 +38,14 @@ from ... import _native as N
 BLOCK = 128
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+_cur_device = getattr(torch._C, "_cuda_getDevice", None)
+
+
 def _stream() -> int:
+    """The current CUDA stream of the current device, as a raw handle."""
+    if _raw_stream is not None and _cur_device is not None:
+        return _raw_stream(_cur_device())
     return torch.cuda.current_stream().cuda_stream
 
 
@@ -70,7 +77,10 @@ class BatchPlan:
     """Device metadata of one ragged batch (page-padded token space).
 
     tokens [R] int32, page_off [R+1] int32, src_blocks/dst_blocks int64 CSR with
-    src_off/dst_off [R+1] int64, round_start and semantic [R] int64.
+    src_off/dst_off [R+1] int64, round_start and semantic [R] int64.  When
+    src_tables/dst_tables (device addresses of the per-request block tables,
+    int64 [R]) are set, src_blocks/dst_blocks are filled on the device by the
+    step's table stage (``gather_tables``) rather than on the host.
     """
 
     num_requests: int
@@ -85,6 +95,9 @@ class BatchPlan:
     semantic: torch.Tensor
     tokens_host: tuple[int, ...]
     max_dst_blocks: int
+    src_tables: torch.Tensor | None = None
+    dst_tables: torch.Tensor | None = None
+    keep_alive: list | None = None  # converted block tables referenced by src/dst_tables
 
     @property
     def tok_total(self) -> int:

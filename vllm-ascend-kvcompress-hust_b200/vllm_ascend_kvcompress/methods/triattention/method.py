@@ -21,6 +21,7 @@ explicit ``check_device_errors``.
 
 from __future__ import annotations
 
+import ctypes
 import os
 from collections.abc import Mapping, Sequence
 from dataclasses import dataclass
@@ -76,14 +77,76 @@ class _Workspaces:
     def __init__(self, device: torch.device) -> None:
         self.device = device
         self._bufs: dict[str, torch.Tensor] = {}
+        self._ptrs: dict[str, tuple[int, int]] = {}
 
-    def get(self, name: str, numel: int, dtype: torch.dtype) -> torch.Tensor:
+    def _buf(self, name: str, numel: int, dtype: torch.dtype) -> torch.Tensor:
         buf = self._bufs.get(name)
         if buf is None or buf.numel() < numel or buf.dtype != dtype:
             cap = max(numel, int(buf.numel() * 1.25) if buf is not None and buf.dtype == dtype else 0, 1)
             buf = torch.empty(cap + 16, dtype=dtype, device=self.device)
             self._bufs[name] = buf
-        return buf[:numel]
+            self._ptrs[name] = (buf.numel(), buf.data_ptr())
+        return buf
+
+    def get(self, name: str, numel: int, dtype: torch.dtype) -> torch.Tensor:
+        return self._buf(name, numel, dtype)[:numel]
+
+    def ptr(self, name: str, numel: int, dtype: torch.dtype) -> int:
+        """Device address of the buffer (grown to ``numel`` elements of ``dtype`` if needed)."""
+        hit = self._ptrs.get(name)
+        if hit is not None and hit[0] >= numel and self._bufs[name].dtype == dtype:
+            return hit[1]
+        return self._buf(name, numel, dtype).data_ptr()
+
+
+class _MetadataStager:
+    """Per-step request metadata: pinned host ring -> one H2D copy -> device views.
+
+    Each step's integers go into the next of ``slots`` pinned host buffers and
+    are copied to the device with a single async copy on the current stream.
+    A host buffer is rewritten only after the copy that last read it has
+    completed (its event), so the host does not wait for the GPU in steady state.
+    """
+
+    def __init__(self, device: torch.device, slots: int = 4) -> None:
+        self.device = device
+        self.slots = slots
+        self.cap = 0
+        self.i = 0
+        self.host: list[torch.Tensor] = []
+        self.events: list[torch.cuda.Event | None] = []
+        self.dev: torch.Tensor | None = None
+
+    def _grow(self, n: int) -> None:
+        for ev in self.events:  # old host buffers may still feed a copy
+            if ev is not None:
+                ev.synchronize()
+        cap = max(n, 2 * self.cap, 256)
+        self.host = [torch.empty(cap, dtype=torch.int64).pin_memory() for _ in range(self.slots)]
+        self.events = [None] * self.slots
+        self.dev = torch.empty(cap, dtype=torch.int64, device=self.device)
+        self.cap = cap
+
+    def stage(self, i64: list[int], i32: list[int]) -> tuple[torch.Tensor, torch.Tensor]:
+        """Device views (int64 [len(i64)], int32 [len(i32)]) of the staged values."""
+        n64 = len(i64)
+        n = n64 + (len(i32) + 1) // 2
+        if n > self.cap:
+            self._grow(n)
+        slot = self.i
+        self.i = (self.i + 1) % self.slots
+        ev = self.events[slot]
+        if ev is not None:
+            ev.synchronize()
+        host = self.host[slot]
+        h = host.numpy()
+        h[:n64] = i64
+        h.view("int32")[2 * n64: 2 * n64 + len(i32)] = i32
+        self.dev[:n].copy_(host[:n], non_blocking=True)
+        if ev is None:
+            ev = self.events[slot] = torch.cuda.Event()
+        ev.record()
+        return self.dev[:n64], self.dev.view(torch.int32)[2 * n64: 2 * n64 + len(i32)]
 
 
 class TriAttentionMethod(KVCompressionMethod):
@@ -103,7 +166,9 @@ class TriAttentionMethod(KVCompressionMethod):
         self.tp_group = None
         self.staged_block_rows: torch.Tensor | None = None
         self.staged_offsets: torch.Tensor | None = None
-        self.profiler = None  # optional object with .mark(name) (bench timing hooks)
+        # optional timing hooks: .mark(name) records a stage boundary now, .add(name, event)
+        # takes an event that the library records at that boundary
+        self.profiler = None
         # "auto": tensor-core scorer where the geometry allows, else the CUDA-core one
         self.scorer = "auto"
         self._ws: _Workspaces | None = None
@@ -175,9 +240,14 @@ class TriAttentionMethod(KVCompressionMethod):
         self._bind_geometry(device)
         self._bind_scoring_tensors()
         self._ws = _Workspaces(device)
+        self._stager = _MetadataStager(device)
         self._err = torch.zeros(1, dtype=torch.int32, device=device)
         self._err_host = torch.zeros(1, dtype=torch.int32).pin_memory()
         self._err_event = None
+        self._err_ev: torch.cuda.Event | None = None
+        self._strict = os.environ.get(_STRICT_ENV, "") == "1"
+        self._last_shape = (0, 0, 0, 0)
+        self._bind_step()
 
     def compress(self, request: CompressionRequest) -> CompressionResult:
         return self.compress_many((request,))[0]
@@ -194,10 +264,9 @@ class TriAttentionMethod(KVCompressionMethod):
         self._raise_pending_device_error()
         plan = self._plan([(r.physical_num_tokens, r.semantic_num_tokens, r.source_block_ids_device,
                             r.destination_block_ids_device) for r in reqs])
-        keep = self._score_and_select(plan)
-        self._compact(plan, keep, stage_commit)
+        self._run_step(plan, compact=True, stage_commit=stage_commit)
         self._arm_error_check()
-        if os.environ.get(_STRICT_ENV, "") == "1":
+        if self._strict:
             self.check_device_errors()
         lengths = tuple((c.name, self.config.kv_budget) for c in self.materialization_caches)
         return tuple(CompressionResult(physical_num_tokens=self.config.kv_budget,
@@ -209,14 +278,16 @@ class TriAttentionMethod(KVCompressionMethod):
         self._require_bound()
         plan = self._plan([(r.physical_num_tokens, r.semantic_num_tokens, r.source_block_ids_device,
                             r.destination_block_ids_device) for r in reqs], need_destination=False)
-        return self._score_and_select(plan).view(len(reqs), self.config.kv_budget).clone()
+        self._run_step(plan, compact=False)
+        return self._keep_view(len(reqs)).view(len(reqs), self.config.kv_budget).clone()
 
     def _select_keep_indices(self, source_block_ids: torch.Tensor, physical_num_tokens: int,
                              round_start: int) -> torch.Tensor:
         """Sorted keep positions of one request (the reference method's private hook)."""
         self._require_bound()
         plan = self._plan([(physical_num_tokens, round_start, source_block_ids, None)], need_destination=False)
-        return self._score_and_select(plan)[: self.config.kv_budget].clone()
+        self._run_step(plan, compact=False)
+        return self._keep_view(1).clone()
 
     def check_device_errors(self) -> None:
         """Synchronise on the last launch and raise if a kernel reported a bad index."""
@@ -330,11 +401,17 @@ class TriAttentionMethod(KVCompressionMethod):
             raise RuntimeError("TriAttention method is not bound to KV cache")
 
     def _plan(self, items, need_destination: bool = True) -> K.BatchPlan:
-        """Validate a batch on the host and stage its metadata on the device."""
+        """Validate a batch on the host and stage its metadata on the device.
+
+        The per-request block tables are not copied here: their device
+        addresses travel with the metadata and the step's first stage gathers
+        them into the CSR arrays ``src_blocks`` / ``dst_blocks``.
+        """
         budget = self.config.kv_budget
         bs = self.cache_block_size
         dev = self.offsets.device
-        tokens, pages, sem, srcs, dsts = [], [], [], [], []
+        tokens, sem, src_ptrs, dst_ptrs, keep_alive = [], [], [], [], []
+        page_off = [0]
         dst_need = -(-budget // bs)
         for t, s, src, dst in items:
             t, s = int(t), int(s)
@@ -343,109 +420,179 @@ class TriAttentionMethod(KVCompressionMethod):
             n = -(-t // bs)
             if src.numel() < n:
                 raise RuntimeError("source block table is shorter than the physical token count")
+            if src.dtype != torch.int64 or src.device != dev or not src.is_contiguous():
+                src = src.to(device=dev, dtype=torch.int64).contiguous()
+                keep_alive.append(src)
             tokens.append(t)
-            pages.append(n)
+            page_off.append(page_off[-1] + n)
             sem.append(s)
-            srcs.append(src.reshape(-1)[:n])
+            src_ptrs.append(src.data_ptr())
             if need_destination:
                 if dst is None or dst.numel() < dst_need:
                     raise RuntimeError("destination block table is shorter than kv_budget")
-                dsts.append(dst.reshape(-1)[:dst_need])
+                if dst.dtype != torch.int64 or dst.device != dev or not dst.is_contiguous():
+                    dst = dst.to(device=dev, dtype=torch.int64).contiguous()
+                    keep_alive.append(dst)
+                dst_ptrs.append(dst.data_ptr())
         R = len(tokens)
-        page_off = [0]
-        for n in pages:
-            page_off.append(page_off[-1] + n)
-        src_off = page_off
-        dst_off = [i * dst_need for i in range(R + 1)] if need_destination else [0] * (R + 1)
-        i32 = torch.tensor(tokens + page_off, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
-        i64 = torch.tensor(src_off + dst_off + sem + sem, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
-        cat = lambda xs: (xs[0] if len(xs) == 1 else torch.cat(xs)).to(device=dev, dtype=torch.int64)
-        src_blocks = cat(srcs)
-        dst_blocks = cat(dsts) if need_destination else src_blocks[:0]
+        dst_off = list(range(0, (R + 1) * dst_need, dst_need)) if need_destination else [0] * (R + 1)
+        i64, i32 = self._stager.stage(page_off + dst_off + sem + sem + src_ptrs + dst_ptrs, tokens + page_off)
+        ws = self._ws
+        src_blocks = ws.get("src_blocks", page_off[-1], torch.int64)
+        dst_blocks = ws.get("dst_blocks", R * dst_need, torch.int64) if need_destination else src_blocks[:0]
+        q = 4 * R + 2
         return K.BatchPlan(
             num_requests=R, total_pages=page_off[-1], tokens=i32[:R], page_off=i32[R:],
             src_blocks=src_blocks, src_off=i64[: R + 1], dst_blocks=dst_blocks, dst_off=i64[R + 1: 2 * R + 2],
-            round_start=i64[2 * R + 2: 3 * R + 2], semantic=i64[3 * R + 2:], tokens_host=tuple(tokens),
-            max_dst_blocks=dst_need)
+            round_start=i64[2 * R + 2: 3 * R + 2], semantic=i64[3 * R + 2: q], tokens_host=tuple(tokens),
+            max_dst_blocks=dst_need, src_tables=i64[q: q + R],
+            dst_tables=i64[q + R: q + 2 * R] if need_destination else None, keep_alive=keep_alive)
 
     def _mark(self, name: str) -> None:
         if self.profiler is not None:
             self.profiler.mark(name)
 
-    def _score_and_select(self, plan: K.BatchPlan) -> torch.Tensor:
-        ws = self._ws
+    def _bind_step(self) -> None:
+        """Fill the bound-once fields of the native step descriptor."""
         cfg = self.config
+        st = N.TriAttentionStep()
+        st.scorer = N.SCORER_TENSOR if self.use_tensor_scorer else N.SCORER_FMA
+        st.kv_dtype = K._dtype_code(self.kv_dtype)
+        st.score_layers = self.scoring_layer_count
+        st.kv_heads = self.local_kv_heads
+        st.group = self.group
+        st.head_dim = self.head_dim
+        st.rotary_dim = self.rotary_dim
+        st.n_off = self.offsets.numel()
+        st.score_aggregation = self.score_aggregation_code
+        st.layer_aggregation = self.layer_aggregation_code
+        st.budget = cfg.kv_budget
+        st.prefix = cfg.protected_prefix_window
+        st.recent = cfg.protected_recent_window
+        st.segments = cfg.position_segments
+        st.policy = N.POLICY_V3 if cfg.position_policy == "v3" else N.POLICY_GLOBAL
+        st.compact_layers = len(self.materialization_caches)
+        st.num_blocks = self.num_blocks
+        st.block_stride = self.block_stride
+        st.block_stride_bytes = self.block_stride_bytes
+        st.row_bytes = self.row_bytes
+        if self.use_tensor_scorer:
+            st.key_maps = ctypes.addressof(self._key_maps)
+            st.q_pass = K._p(self.scoring_q_pass)
+        st.score_k = ctypes.addressof(self._k_score)
+        st.k_layers = ctypes.addressof(self._k_all)
+        st.v_layers = ctypes.addressof(self._v_all)
+        st.omega = self.scoring_omega.data_ptr()
+        st.offsets = self.offsets.data_ptr()
+        st.q_real = self.scoring_q_real.data_ptr()
+        st.q_imag = self.scoring_q_imag.data_ptr()
+        st.scale = self.scoring_scale.data_ptr()
+        st.extra = self.scoring_extra.data_ptr()
+        st.q_pass_t = K._p(self.scoring_q_pass_t)
+        st.error_flag = self._err.data_ptr()
+        self._step = st
+        self._step_ref = ctypes.byref(st)
+
+    def _launch(self, stages: int, slots) -> None:
+        """kvc_triattention_run on the current stream (with stage events when profiled)."""
+        events = None
+        prof = self.profiler
+        if prof is not None and getattr(prof, "active", True):
+            events = (ctypes.c_void_p * N.STEP_EVENTS)()
+            for i in slots:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()  # creates the event; the library records it again at its stage boundary
+                events[i] = ev.cuda_event
+                prof.add(N.STEP_EVENT_NAMES[i], ev)
+        N.check(N.lib().kvc_triattention_run(self._step_ref, stages, events, K._stream()), "kvc_triattention_run")
+
+    def _set_plan(self, plan: K.BatchPlan) -> N.TriAttentionStep:
+        """Point the step descriptor at one batch's device metadata."""
+        st = self._step
+        st.num_requests = plan.num_requests
+        st.total_pages = plan.total_pages
+        st.tokens = plan.tokens.data_ptr()
+        st.page_off = plan.page_off.data_ptr()
+        st.src_blocks = plan.src_blocks.data_ptr()
+        st.src_block_off = plan.src_off.data_ptr()
+        st.dst_blocks = plan.dst_blocks.data_ptr()
+        st.dst_block_off = plan.dst_off.data_ptr()
+        st.round_start = plan.round_start.data_ptr()
+        st.semantic = plan.semantic.data_ptr()
+        st.src_tables = plan.src_tables.data_ptr()
+        st.dst_tables = K._p(plan.dst_tables)
+        return st
+
+    def _gather_tables(self, plan: K.BatchPlan) -> None:
+        """Fill plan.src_blocks / plan.dst_blocks on the device (the step's table stage alone)."""
+        self._set_plan(plan)
+        N.check(N.lib().kvc_triattention_run(self._step_ref, N.STAGE_TABLES, None, K._stream()),
+                "kvc_triattention_run")
+
+    def _run_step(self, plan: K.BatchPlan, *, compact: bool, stage_commit: bool = False) -> None:
+        """Score, select and (optionally) compact one batch (keep indices land in the "keep" workspace)."""
+        ws = self._ws
         L = self.scoring_layer_count
         heads = self.local_kv_heads * self.group
         R, tok = plan.num_requests, plan.tok_total
         parts = 4 if self.use_tensor_scorer else 1
-        raw = ws.get("raw", L * heads * tok, torch.float32)
-        partial = ws.get("partial", L * plan.total_pages * parts * heads * 2, torch.float32)
-        mean = ws.get("mean", L * R * heads, torch.float32)
-        var = ws.get("var", L * R * heads, torch.float32)
-        den = ws.get("den", L * R * heads, torch.float32)
-        agg = ws.get("agg", tok, torch.float32)
-        keep = ws.get("keep", R * cfg.kv_budget, torch.int64)
-        self._mark("prepare")
+        st = self._set_plan(plan)
+        f32, i64 = torch.float32, torch.int64
         if self.use_tensor_scorer:
-            frag = ws.get("frag", R * L * self.local_kv_heads * self.frag_block, torch.int32)
-            K.prepare_score_fragments(self.scoring_omega, self.offsets, plan, self.scoring_q_real,
-                                      self.scoring_q_imag, self.scoring_scale, self.scoring_extra,
-                                      self.scoring_q_pass, self.kv_dtype, frag)
-            self._mark("score")
-            K.score_paged_keys_tc(self._key_maps, L, self.kv_dtype, self.num_blocks, self.local_kv_heads,
-                                  self.group, self.head_dim, self.rotary_dim, plan, frag, raw, partial, self._err)
+            st.score_coef = ws.ptr("frag", R * L * self.local_kv_heads * self.frag_block, torch.int32)
         else:
-            coef = ws.get("coef", R * L * self.local_kv_heads * self.coef_block, torch.float32)
-            K.prepare_score_coefficients(self.scoring_omega, self.offsets, plan, self.scoring_q_real,
-                                         self.scoring_q_imag, self.scoring_scale, self.scoring_extra,
-                                         self.score_aggregation_code, coef)
-            self._mark("score")
-            K.score_paged_keys(self._k_score, self.kv_dtype, self.block_stride, self.num_blocks,
-                               self.local_kv_heads, self.group, self.head_dim, self.rotary_dim, plan, coef,
-                               self.offsets.numel(), self.score_aggregation_code, self.scoring_q_pass_t, raw,
-                               partial, self._err)
-        self._mark("head_stats")
-        K.head_stats(partial, L, heads, plan, mean, var, den, parts)
-        self._mark("normalize")
-        rows = ws.get("rows", L * tok, torch.float32)
+            st.score_coef = ws.ptr("coef", R * L * self.local_kv_heads * self.coef_block, f32)
+        st.raw = ws.ptr("raw", L * heads * tok, f32)
+        st.partial = ws.ptr("partial", L * plan.total_pages * parts * heads * 2, f32)
+        st.mean = ws.ptr("mean", L * R * heads, f32)
+        st.var = ws.ptr("var", L * R * heads, f32)
+        st.den = ws.ptr("den", L * R * heads, f32)
+        st.rows = ws.ptr("rows", L * tok, f32)
+        st.agg = ws.ptr("agg", tok, f32)
+        st.keep = ws.ptr("keep", R * self.config.kv_budget, i64)
+        self._last_shape = (L, R, heads, tok)
+        staged_rows = staged_off = None
+        if compact and stage_commit:
+            staged_rows = ws.get("staged_rows", R * plan.max_dst_blocks, torch.int64).view(R, plan.max_dst_blocks)
+            staged_off = ws.get("staged_off", R, torch.int64)
+        st.staged_rows = K._p(staged_rows)
+        st.staged_row_stride = plan.max_dst_blocks
+        st.staged_offsets = K._p(staged_off)
+        tail = N.STAGE_AGGREGATE | N.STAGE_SELECT | (N.STAGE_COMPACT if compact else 0)
+        tail_slots = (4, 5, 6, 7) if compact else (4, 5, 7)
+        head = N.STAGE_TABLES | N.STAGE_SCORE
         if self.tensor_parallel_size > 1:
-            K.normalize_aggregate(raw, L, heads, plan, mean, den, self.layer_aggregation_code, rows_out=rows)
+            self._launch(head, (0, 1, 2, 3))
             self._mark("tp_sync")
-            self._tp_all_reduce_max(rows)
-            self._mark("aggregate_rows")
-            K.aggregate_rows(rows, L, plan, self.layer_aggregation_code, agg)
+            self._tp_all_reduce_max(ws.get("rows", L * tok, f32))
+            self._launch(tail, tail_slots)
         else:
-            K.normalize_aggregate(raw, L, heads, plan, mean, den, self.layer_aggregation_code, rows_out=rows,
-                                  agg_out=agg)
-        self._mark("select")
-        policy = N.POLICY_V3 if cfg.position_policy == "v3" else N.POLICY_GLOBAL
-        K.select_keep(agg, plan, cfg.kv_budget, cfg.protected_prefix_window, cfg.protected_recent_window,
-                      cfg.position_segments, policy, keep, self._err)
-        self.last_stats = (raw, mean, var, agg)  # views of workspaces, for inspection/tests
-        return keep
+            self._launch(head | tail, (0, 1, 2, 3, *tail_slots))
+        if compact:
+            self.staged_block_rows, self.staged_offsets = staged_rows, staged_off
+
+    @property
+    def last_stats(self) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+        """(raw, mean, var, agg) workspace views of the last step, for inspection and tests."""
+        L, R, heads, tok = self._last_shape
+        ws = self._ws
+        return (ws.get("raw", L * heads * tok, torch.float32), ws.get("mean", L * R * heads, torch.float32),
+                ws.get("var", L * R * heads, torch.float32), ws.get("agg", tok, torch.float32))
+
+    def _keep_view(self, R: int) -> torch.Tensor:
+        return self._ws.get("keep", R * self.config.kv_budget, torch.int64)
 
     def _tp_all_reduce_max(self, rows: torch.Tensor) -> None:
         tp_score_sync(rows, self.tp_group)
-
-    def _compact(self, plan: K.BatchPlan, keep: torch.Tensor, stage_commit: bool) -> None:
-        staged_rows = staged_off = None
-        if stage_commit:
-            staged_rows = self._ws.get("staged_rows", plan.num_requests * plan.max_dst_blocks, torch.int64
-                                       ).view(plan.num_requests, plan.max_dst_blocks)
-            staged_off = self._ws.get("staged_off", plan.num_requests, torch.int64)
-        self._mark("compact")
-        K.compact(self._k_all, self._v_all, self.block_stride_bytes, self.num_blocks, self.row_bytes, plan, keep,
-                  self.config.kv_budget, self._err, staged_rows, staged_off)
-        self._mark("end")
-        self.staged_block_rows, self.staged_offsets = staged_rows, staged_off
 
     # ---- device error reporting ---------------------------------------------
 
     def _arm_error_check(self) -> None:
         self._err_host.copy_(self._err, non_blocking=True)
-        self._err_event = torch.cuda.Event()
-        self._err_event.record()
+        if self._err_ev is None:
+            self._err_ev = torch.cuda.Event()
+        self._err_ev.record()
+        self._err_event = self._err_ev
 
     def _raise_pending_device_error(self) -> None:
         ev = self._err_event
