@@ -101,12 +101,12 @@ class StageTimer:
             self.steps[-1].append((name, ev))
 
     def stage_ms(self) -> dict[str, float]:
-        """Average duration of each stage (from its mark to the next mark)."""
+        """Median duration of each stage (from its mark to the next mark) over the steps."""
         acc: dict[str, list[float]] = {}
         for marks in self.steps:
             for (name, a), (_, b) in zip(marks, marks[1:]):
                 acc.setdefault(name, []).append(a.elapsed_time(b))
-        return {k: sum(v) / len(v) for k, v in acc.items()}
+        return {k: sorted(v)[len(v) // 2] for k, v in acc.items()}
 
 
 class ClockSampler:
@@ -326,7 +326,10 @@ def b200_arm(args) -> None:
     barrier()
     clk = clocks.stop()
     m.check_device_errors()
-    # per-stage breakdown: a separate, instrumented pass (stage events cost host time)
+    # per-stage breakdown: a separate, instrumented pass (stage events cost host time),
+    # started together on all ranks so the first sync does not absorb their skew
+    torch.cuda.synchronize()
+    barrier()
     m.profiler = timer
     timer.active = True
     for _ in range(max(3, min(args.steps, 20))):
@@ -397,7 +400,9 @@ def b200_arm(args) -> None:
         tf = ROOT / "profiles" / "traffic.json"
         if tf.is_file() and args.config == 1 and args.seqs == 32 and args.layers == 48:
             traffic = json.loads(tf.read_text()).get("compact_kernel_bytes_per_launch_config1")
-        launches_per_step = 7  # prepare, score, head_stats, normalize, aggregate_rows, select, compact
+        # block-table gather, prepare, score, head_stats, normalize, then aggregate_rows (TP=1 / NCCL)
+        # or the two exchange kernels (peer sync), select, compact
+        launches_per_step = 9 if m.tp_sync_mode == "peer" else 8
         step_bytes = sum(ab.values())
         line = {
             "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -414,6 +419,7 @@ def b200_arm(args) -> None:
             "stages_ms": stages,
             "score_kernel": {"achieved": score_gbs, "frac": score_gbs / peak, "algorithmic_bytes": ab["score"]},
             "tp_sync_us": stages.get("tp_sync", 0.0) * 1e3 if world > 1 else None,
+            "tp_sync_path": m.tp_sync_mode,
             "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                     "path": "TriAttentionMethod.compress_many(stage_commit=True): pinned H2D block tables, "

@@ -268,6 +268,54 @@ int kvc_shift_positions(const int64_t* positions, const void* request_indices, i
                         int32_t* error_flag, void* stream);
 
 /*
+ * Tensor-parallel score sync over NVLink peer memory, replacing the MAX
+ * all-reduce of the per-layer rows and the layer reduction after it (the
+ * dist.all_reduce(parallel_scores, MAX) of TriAttentionMethod._select_keep_indices
+ * and the sum/amax, division and nan_to_num that follow,
+ * methods/triattention/method.py:447-467).
+ *
+ * Every rank of the TP group calls it once per step on its stream, with the
+ * same world, layers, pages, requests and epoch.  peer_rows[p] is rank p's
+ * rows buffer ([L][total_pages*128] fp32, the kvc_normalize_aggregate rows of
+ * its local heads), peer_agg[p] its agg buffer ([total_pages*128]) and
+ * peer_flags[p] its flag words (kvc_tp_exchange_flag_words(world) int32,
+ * zero-initialised once); the three are device arrays of `world` device
+ * addresses valid on this GPU (this rank's own buffers at index `rank`, the
+ * others mapped with kvc_ipc_open); every rows/agg buffer 16-byte aligned
+ * (the kernel moves 4 tokens per access).  On return (stream order) every rank's
+ * agg holds the finalised scores of the whole step: the max over ranks of each
+ * layer's row (NaN-propagating), reduced over layers (sequential sum then / L,
+ * or max) and mapped NaN -> -inf, +inf -> 1e30; page padding is 0.  This is
+ * bit-identical to kvc_aggregate_rows applied to the TP=1 rows.
+ * epoch: a positive step counter, one larger on every call (flags are never
+ * cleared).  Waits for other ranks are bounded (2 s); on expiry the kernels
+ * raise KVC_DEV_TIMEOUT in error_flag and complete.
+ * The rows and agg buffers must not be rewritten by the caller until the call
+ * has completed on this rank's stream (the next step's normalisation is safe).
+ */
+#define KVC_TP_MAX_WORLD 64
+int kvc_tp_exchange_flag_words(int world);
+int kvc_tp_exchange_max(const float* const* peer_rows, float* const* peer_agg, int32_t* const* peer_flags,
+                        int world, int rank, int num_layers, int total_pages, const int32_t* tokens,
+                        const int32_t* page_off, int num_requests, int layer_aggregation, int32_t epoch,
+                        int32_t* error_flag, void* stream);
+
+/*
+ * CUDA IPC for the exchange buffers (no reference counterpart; the reference
+ * syncs through HCCL).  kvc_ipc_export gives the handle of the allocation that
+ * holds `ptr` (KVC_IPC_HANDLE_BYTES) and ptr's offset inside it; another
+ * process opens the handle with kvc_ipc_open (base of the allocation on its
+ * device) and adds the offset.  Memory from cudaMalloc-backed allocators only
+ * (not virtual-memory-managed pools).  kvc_can_access_peer reports whether
+ * `device` can load/store `peer`'s memory directly.
+ */
+#define KVC_IPC_HANDLE_BYTES 64
+int kvc_ipc_export(int device, const void* ptr, void* handle_out, int64_t* offset_out);
+int kvc_ipc_open(int device, const void* handle, void** base_out);
+int kvc_ipc_close(int device, void* base);
+int kvc_can_access_peer(int device, int peer);
+
+/*
  * One compression step in a single call.
  *
  * No reference counterpart: the reference issues each device op from Python

@@ -1,0 +1,101 @@
+"""The peer-memory TP exchange kernel through the C ABI on one GPU.
+
+world = 1 runs the whole data path (signal, reduce, layer reduction, push,
+wait) against this rank's own buffers and must equal kvc_aggregate_rows bit
+for bit.  A world-2 call whose other rank never arrives must give up after
+its bounded wait, report KVC_DEV_TIMEOUT and leave the context usable.  The
+two-GPU exchange is covered by test_gpu_tp_nccl.py.
+"""
+
+from __future__ import annotations
+
+import time
+
+import pytest
+import torch
+
+from vllm_ascend_kvcompress import _native as N
+
+pytestmark = pytest.mark.gpu
+
+
+def _meta(lengths):
+    pages = [-(-t // 128) for t in lengths]
+    off = [0]
+    for p in pages:
+        off.append(off[-1] + p)
+    tokens = torch.tensor(lengths, dtype=torch.int32, device="cuda")
+    page_off = torch.tensor(off, dtype=torch.int32, device="cuda")
+    return tokens, page_off, off[-1]
+
+
+def _buffers(world, layers, tok):
+    words = N.lib().kvc_tp_exchange_flag_words(world)
+    rows = [torch.empty(layers * tok, device="cuda") for _ in range(world)]
+    agg = [torch.full((tok,), 7.0, device="cuda") for _ in range(world)]
+    flags = [torch.zeros(words, dtype=torch.int32, device="cuda") for _ in range(world)]
+    table = lambda ts: torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device="cuda")
+    return rows, agg, flags, table(rows), table(agg), table(flags)
+
+
+@pytest.mark.parametrize("layer_agg", [N.AGG_MEAN, N.AGG_MAX])
+def test_single_rank_exchange_equals_aggregate_rows_bitwise(layer_agg):
+    lib = N.lib()
+    lengths = [300, 1, 128, 2049]
+    tokens, page_off, pages = _meta(lengths)
+    tok, L = pages * 128, 5
+    rows, agg, flags, t_rows, t_agg, t_flags = _buffers(1, L, tok)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    rows[0].copy_(torch.randn(L * tok, generator=g, device="cuda") * 3)
+    rows[0][17] = float("nan")
+    rows[0][tok + 40] = float("inf")
+    rows[0][2 * tok + 41] = float("-inf")
+    ref = torch.full((tok,), 3.0, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.kvc_aggregate_rows(rows[0].data_ptr(), L, pages, tokens.data_ptr(), page_off.data_ptr(),
+                                  len(lengths), layer_agg, ref.data_ptr(), stream) == 0
+    for epoch in (1, 2):  # two steps in a row: epochs advance, flags are never cleared
+        agg[0].fill_(7.0)
+        assert lib.kvc_tp_exchange_max(t_rows.data_ptr(), t_agg.data_ptr(), t_flags.data_ptr(), 1, 0, L, pages,
+                                       tokens.data_ptr(), page_off.data_ptr(), len(lengths), layer_agg, epoch,
+                                       err.data_ptr(), stream) == 0
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        assert torch.equal(agg[0].view(torch.int32), ref.view(torch.int32))
+    assert flags[0].tolist() == [2, 2, 0]
+
+
+def test_exchange_rejects_bad_arguments_on_the_host():
+    lib = N.lib()
+    tokens, page_off, pages = _meta([256])
+    _, _, _, t_rows, t_agg, t_flags = _buffers(1, 1, pages * 128)
+    s = torch.cuda.current_stream().cuda_stream
+    args = lambda world, rank, epoch: (t_rows.data_ptr(), t_agg.data_ptr(), t_flags.data_ptr(), world, rank, 1,
+                                       pages, tokens.data_ptr(), page_off.data_ptr(), 1, N.AGG_MEAN, epoch, None, s)
+    assert lib.kvc_tp_exchange_max(*args(1, 1, 1)) == -22  # rank outside the world
+    assert lib.kvc_tp_exchange_max(*args(0, 0, 1)) == -22
+    assert lib.kvc_tp_exchange_max(*args(1, 0, 0)) == -22  # epochs start at 1
+
+
+def test_absent_rank_times_out_with_an_error_status():
+    """Rank 1 never arrives: both bounded waits expire, the flag reports it, the GPU stays usable."""
+    lib = N.lib()
+    tokens, page_off, pages = _meta([1000])
+    tok = pages * 128
+    rows, agg, flags, t_rows, t_agg, t_flags = _buffers(2, 2, tok)
+    for r in rows:
+        r.zero_()
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    t0 = time.perf_counter()
+    assert lib.kvc_tp_exchange_max(t_rows.data_ptr(), t_agg.data_ptr(), t_flags.data_ptr(), 2, 0, 2, pages,
+                                   tokens.data_ptr(), page_off.data_ptr(), 1, N.AGG_MEAN, 1, err.data_ptr(),
+                                   torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    assert int(err.item()) & N.DEV_TIMEOUT
+    assert 1.5 < waited < 30
+    # this rank announced itself to the absent one and then gave up
+    assert flags[1].tolist()[0] == 1 and flags[1].tolist()[2] == 1
+    x = torch.arange(10, device="cuda")
+    assert int(x.sum()) == 45

@@ -21,6 +21,8 @@ STATUS = {0: "ok", -22: "EINVAL", -14: "ENULL", -71: "EALIGN", -95: "EUNSUPPORTE
 CALIB_STATIC_SCRATCH_DOUBLES = 1 << 20
 DEV_BLOCK_RANGE, DEV_TOKEN_RANGE, DEV_BUDGET, DEV_TIMEOUT = 1, 2, 4, 8
 TENSOR_MAP_BYTES = 128
+IPC_HANDLE_BYTES = 64
+TP_MAX_WORLD = 64
 BF16, FP16 = 0, 1
 AGG_MEAN, AGG_MAX = 0, 1
 POLICY_GLOBAL, POLICY_V3 = 0, 1
@@ -58,6 +60,13 @@ _SIGNATURES = {
     "kvc_shift_positions": (c_int, [_P, _P, c_int, _P, c_int64, c_int64, _P, _P, _P]),
     "kvc_calibration_accumulate_noalloc": (
         c_int, [_P, c_int, c_int64, c_int64, c_int, c_int, c_int, _P, _P, _P, _P, _P]),
+    "kvc_tp_exchange_flag_words": (c_int, [c_int]),
+    "kvc_tp_exchange_max": (
+        c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, _P, _P, c_int, c_int, c_int32, _P, _P]),
+    "kvc_ipc_export": (c_int, [c_int, _P, _P, _P]),
+    "kvc_ipc_open": (c_int, [c_int, _P, _P]),
+    "kvc_ipc_close": (c_int, [c_int, _P]),
+    "kvc_can_access_peer": (c_int, [c_int, c_int]),
     "kvc_triattention_step_size": (c_int64, []),
     "kvc_triattention_run": (c_int, [_P, c_int, _P, _P]),
 }

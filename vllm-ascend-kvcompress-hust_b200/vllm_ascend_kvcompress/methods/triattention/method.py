@@ -43,6 +43,7 @@ from . import kernels as K
 from .config import TriAttentionConfig
 from .scoring import build_geometric_offsets
 from .stats import CalibrationStats, DeviceLayerCalibrationStats
+from .tp_exchange import PeerScoreExchange, choose_tp_sync_mode
 
 METHOD_NAME = "triattention"
 _STRICT_ENV = "KVC_B200_STRICT"
@@ -164,6 +165,7 @@ class TriAttentionMethod(KVCompressionMethod):
         self.tensor_parallel_size = 1
         self.tensor_parallel_rank = 0
         self.tp_group = None
+        self._peer: PeerScoreExchange | None = None
         self.staged_block_rows: torch.Tensor | None = None
         self.staged_offsets: torch.Tensor | None = None
         # optional timing hooks: .mark(name) records a stage boundary now, .add(name, event)
@@ -205,8 +207,10 @@ class TriAttentionMethod(KVCompressionMethod):
         N.lib()  # fail at bind time if the native library is missing
         self.tensor_parallel_size = int(self.vllm_config.parallel_config.tensor_parallel_size)
         self.tensor_parallel_rank = 0
+        self._peer = None
         if self.tensor_parallel_size > 1:
             self.tp_group, self.tensor_parallel_rank = self._resolve_tp_group(runner)
+            self._peer = self._bind_peer_exchange(device)
         stats = self.calibration.to_device(
             self.model_shape, device, tensor_parallel_rank=self.tensor_parallel_rank,
             tensor_parallel_size=self.tensor_parallel_size)
@@ -321,6 +325,17 @@ class TriAttentionMethod(KVCompressionMethod):
 
         tp = get_tp_group()
         return tp.device_group, int(tp.rank_in_group)
+
+    def _bind_peer_exchange(self, device: torch.device):
+        """Peer-memory score sync when the TP group is an NCCL group of GPUs that can reach each other."""
+        import torch.distributed as dist
+
+        group = self.tp_group
+        if group is None or not dist.is_initialized() or dist.get_backend(group) != "nccl":
+            return None
+        if choose_tp_sync_mode(group, device.index) != "peer":
+            return None
+        return PeerScoreExchange(group, self.tensor_parallel_rank, self.tensor_parallel_size, device)
 
     def _bind_geometry(self, device: torch.device) -> None:
         caches = self.materialization_caches
@@ -561,7 +576,19 @@ class TriAttentionMethod(KVCompressionMethod):
         tail = N.STAGE_AGGREGATE | N.STAGE_SELECT | (N.STAGE_COMPACT if compact else 0)
         tail_slots = (4, 5, 6, 7) if compact else (4, 5, 7)
         head = N.STAGE_TABLES | N.STAGE_SCORE
-        if self.tensor_parallel_size > 1:
+        ex = self._peer
+        if ex is not None:
+            # rows go straight into the peer-mapped exchange buffer; the exchange
+            # kernel replaces the all-reduce and the layer reduction
+            ex.ensure(L, tok)
+            st.rows = ex.rows_ptr
+            st.agg = ex.agg_ptr
+            self._launch(head, (0, 1, 2, 3))
+            self._mark("tp_sync")
+            ex.exchange(L, plan.total_pages, plan.tokens, plan.page_off, R, self.layer_aggregation_code, self._err,
+                        K._stream())
+            self._launch(tail & ~N.STAGE_AGGREGATE, tail_slots[1:])
+        elif self.tensor_parallel_size > 1:
             self._launch(head, (0, 1, 2, 3))
             self._mark("tp_sync")
             self._tp_all_reduce_max(ws.get("rows", L * tok, f32))
@@ -576,14 +603,22 @@ class TriAttentionMethod(KVCompressionMethod):
         """(raw, mean, var, agg) workspace views of the last step, for inspection and tests."""
         L, R, heads, tok = self._last_shape
         ws = self._ws
+        agg = self._peer.agg_view(tok) if self._peer is not None else ws.get("agg", tok, torch.float32)
         return (ws.get("raw", L * heads * tok, torch.float32), ws.get("mean", L * R * heads, torch.float32),
-                ws.get("var", L * R * heads, torch.float32), ws.get("agg", tok, torch.float32))
+                ws.get("var", L * R * heads, torch.float32), agg)
 
     def _keep_view(self, R: int) -> torch.Tensor:
         return self._ws.get("keep", R * self.config.kv_budget, torch.int64)
 
     def _tp_all_reduce_max(self, rows: torch.Tensor) -> None:
         tp_score_sync(rows, self.tp_group)
+
+    @property
+    def tp_sync_mode(self) -> str:
+        """"peer" (NVLink exchange kernel), "nccl" (MAX all-reduce) or "none" (TP=1)."""
+        if self.tensor_parallel_size == 1:
+            return "none"
+        return "peer" if self._peer is not None else "nccl"
 
     # ---- device error reporting ---------------------------------------------
 
