@@ -35,6 +35,10 @@ struct CompactArgs {
 
 template <int VEC>
 struct Vec;
+struct alignas(32) U32x8 {
+  uint32_t w[8];
+};
+template <> struct Vec<32> { using T = U32x8; };
 template <> struct Vec<16> { using T = uint4; };
 template <> struct Vec<8> { using T = uint2; };
 template <> struct Vec<4> { using T = uint32_t; };
@@ -43,8 +47,30 @@ template <> struct Vec<2> { using T = uint16_t; };
 template <int VEC>
 __device__ __forceinline__ typename Vec<VEC>::T load_nc(const void* p) {
   using T = typename Vec<VEC>::T;
-  if constexpr (VEC == 16) return ldg_stream16(p);
-  else return __ldg(reinterpret_cast<const T*>(p));
+  if constexpr (VEC == 32) {  // one 256-bit load (sm_100)
+    T r;
+    asm("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+        : "=r"(r.w[0]), "=r"(r.w[1]), "=r"(r.w[2]), "=r"(r.w[3]), "=r"(r.w[4]), "=r"(r.w[5]), "=r"(r.w[6]),
+          "=r"(r.w[7])
+        : "l"(p));
+    return r;
+  } else if constexpr (VEC == 16) {
+    return ldg_stream16(p);
+  } else {
+    return __ldg(reinterpret_cast<const T*>(p));
+  }
+}
+
+template <int VEC>
+__device__ __forceinline__ void store_vec(void* p, const typename Vec<VEC>::T& x) {
+  using T = typename Vec<VEC>::T;
+  if constexpr (VEC == 32) {
+    asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(x.w[0]), "r"(x.w[1]),
+                 "r"(x.w[2]), "r"(x.w[3]), "r"(x.w[4]), "r"(x.w[5]), "r"(x.w[6]), "r"(x.w[7])
+                 : "memory");
+  } else {
+    *reinterpret_cast<T*>(p) = x;
+  }
 }
 
 // Resolve (src, dst) byte addresses of output row q; nullptr on a range fault.
@@ -93,7 +119,7 @@ __global__ void __launch_bounds__(kCopyThreads, SMALL ? 3 : 4) compact_kernel(co
     if constexpr (SMALL) {
       // rows narrower than 2 KB: spread the tile's (row, vector) pairs over the
       // lanes so that every lane keeps kSmallU vectors in flight
-      constexpr int kSmallU = 8;
+      constexpr int kSmallU = VEC == 32 ? 4 : 8;  // 128 (256) bytes in flight per lane
       const int total = nrows * nvec;
       for (int e0 = 0; e0 < total; e0 += 32 * kSmallU) {
         T x[kSmallU];
@@ -113,9 +139,10 @@ __global__ void __launch_bounds__(kCopyThreads, SMALL ? 3 : 4) compact_kernel(co
         }
 #pragma unroll
         for (int u = 0; u < kSmallU; ++u)
-          if (dd[u]) *reinterpret_cast<T*>(dd[u]) = x[u];
+          if (dd[u]) store_vec<VEC>(dd[u], x[u]);
       }
     } else {
+    constexpr int kU = VEC == 32 ? 2 : 4;  // vectors per lane per row in one pass
     for (int k = 0; k < nrows; k += 2) {
       const char* s0 = (const char*)__shfl_sync(0xffffffffu, (unsigned long long)my_src, k);
       char* d0 = (char*)__shfl_sync(0xffffffffu, (unsigned long long)my_dst, k);
@@ -123,10 +150,10 @@ __global__ void __launch_bounds__(kCopyThreads, SMALL ? 3 : 4) compact_kernel(co
       const char* s1 = (const char*)__shfl_sync(0xffffffffu, (unsigned long long)my_src, k1);
       char* d1 = (char*)__shfl_sync(0xffffffffu, (unsigned long long)my_dst, k1);
       if (k1 == k) { s1 = nullptr; d1 = nullptr; }
-      for (int v0 = 0; v0 < nvec; v0 += 32 * 4) {
-        T x0[4], x1[4];
+      for (int v0 = 0; v0 < nvec; v0 += 32 * kU) {
+        T x0[kU], x1[kU];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kU; ++u) {
           const int v = v0 + u * 32 + lane;
           if (v < nvec) {
             if (s0) x0[u] = load_nc<VEC>(s0 + (int64_t)v * VEC);
@@ -134,11 +161,11 @@ __global__ void __launch_bounds__(kCopyThreads, SMALL ? 3 : 4) compact_kernel(co
           }
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kU; ++u) {
           const int v = v0 + u * 32 + lane;
           if (v < nvec) {
-            if (s0) *reinterpret_cast<T*>(d0 + (int64_t)v * VEC) = x0[u];
-            if (s1) *reinterpret_cast<T*>(d1 + (int64_t)v * VEC) = x1[u];
+            if (s0) store_vec<VEC>(d0 + (int64_t)v * VEC, x0[u]);
+            if (s1) store_vec<VEC>(d1 + (int64_t)v * VEC, x1[u]);
           }
         }
       }
@@ -261,7 +288,8 @@ extern "C" int kvc_compact(const void* const* k_layers, const void* const* v_lay
     KVC_CHECK_ARG(k_layers[i] && v_layers[i], KVC_ENULL);
     bits |= (uintptr_t)k_layers[i] | (uintptr_t)v_layers[i];
   }
-  const int vec = vec_width(bits);
+  // 32-byte vectors (256-bit loads/stores) when every base, stride and row allows them
+  const int vec = bits % 32 == 0 ? 32 : vec_width(bits);
   KVC_CHECK_ARG(vec > 0, KVC_EALIGN);
   for (int l0 = 0; l0 < N; l0 += kMaxCompactLayers) {
     CompactArgs a{};
@@ -289,8 +317,9 @@ extern "C" int kvc_compact(const void* const* k_layers, const void* const* v_lay
     const int64_t nvec = row_bytes / vec;
     a.nvec_shift = (nvec & (nvec - 1)) == 0 ? __builtin_ctzll((unsigned long long)nvec) : -1;
     const int64_t tiles = (rows + a.tile_rows - 1) / a.tile_rows;
-    if (nvec < 128) {
+    if (row_bytes < 2048) {
       switch (vec) {
+        case 32: launch_compact<32, true>(a, tiles, st); break;
         case 16: launch_compact<16, true>(a, tiles, st); break;
         case 8: launch_compact<8, true>(a, tiles, st); break;
         case 4: launch_compact<4, true>(a, tiles, st); break;
@@ -298,6 +327,7 @@ extern "C" int kvc_compact(const void* const* k_layers, const void* const* v_lay
       }
     } else {
       switch (vec) {
+        case 32: launch_compact<32, false>(a, tiles, st); break;
         case 16: launch_compact<16, false>(a, tiles, st); break;
         case 8: launch_compact<8, false>(a, tiles, st); break;
         case 4: launch_compact<4, false>(a, tiles, st); break;
