@@ -269,3 +269,40 @@ def test_calibration_partial_rope_unaligned_widths():
     torch.testing.assert_close(acc.real_sum.float().cpu(), ref.real_sum, rtol=1e-5, atol=1e-4)
     torch.testing.assert_close(acc.abs_sum.float().cpu(), ref.abs_sum, rtol=1e-5, atol=1e-4)
     torch.testing.assert_close(acc.pass_sum.float().cpu(), ref.pass_sum, rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("heads", [1, 3, 5, 40])
+def test_normalize_rows_equal_torch_fp32_bitwise(heads):
+    """kvc_normalize_aggregate rows == max over heads of (raw - mean) / den in IEEE fp32 (torch), padding 0."""
+    lib = N.lib()
+    lengths = [1, 300, 2049, 128, 5000]
+    pages = [-(-t // 128) for t in lengths]
+    off = [0]
+    for p in pages:
+        off.append(off[-1] + p)
+    P, L, R = off[-1], 3, len(lengths)
+    g = torch.Generator(device="cuda").manual_seed(heads)
+    raw = torch.randn(L, P, heads, 128, generator=g, device="cuda") * 5 + 2
+    raw[0, 3, 0, 7] = float("nan")
+    raw[1, 2, heads - 1, 9] = float("inf")
+    raw[2, 5, 0, 0] = float("-inf")
+    mean = torch.randn(L, R, heads, generator=g, device="cuda")
+    den = torch.rand(L, R, heads, generator=g, device="cuda") * 3 + 1e-3
+    tokens = torch.tensor(lengths, dtype=torch.int32, device="cuda")
+    page_off = torch.tensor(off, dtype=torch.int32, device="cuda")
+    rows = torch.full((L, P * 128), 123.0, device="cuda")
+    assert lib.kvc_normalize_aggregate(raw.data_ptr(), L, heads, P, mean.data_ptr(), den.data_ptr(),
+                                       tokens.data_ptr(), page_off.data_ptr(), R, N.AGG_MEAN, rows.data_ptr(),
+                                       None, torch.cuda.current_stream().cuda_stream) == 0
+    req = torch.repeat_interleave(torch.arange(R, device="cuda"), torch.tensor(pages, device="cuda"))  # per page
+    mu = mean[:, req, :, None]  # [L, P, heads, 1]
+    dn = den[:, req, :, None]
+    ref = ((raw - mu) / dn).amax(dim=2).reshape(L, P * 128)
+    pos = torch.arange(128, device="cuda").repeat(P) + 0
+    valid = pos + (torch.arange(P, device="cuda") - page_off[req].long()).repeat_interleave(128) * 128 \
+        < tokens[req].long().repeat_interleave(128)
+    ref = torch.where(valid[None], ref, torch.zeros_like(ref))
+    torch.cuda.synchronize()
+    nan = torch.isnan(ref)
+    assert nan.any() and torch.equal(torch.isnan(rows), nan)
+    assert torch.equal(rows[~nan].view(torch.int32), ref[~nan].view(torch.int32))

@@ -436,58 +436,89 @@ __device__ __forceinline__ float div_by(float a, float b, float rcp) {
   return __fmaf_rn(r, rcp, q0);
 }
 
-// Grid (token blocks, scoring layers): one thread per (token, layer).  A CTA
-// covers 256 tokens = two pages, hence at most two requests; their per-head
-// mean and denominator for this layer are staged in shared memory.  The
-// thread writes the layer's head-max row; aggregate_rows then reduces the
-// layers (the same path serves TP=1 and the TP all-reduce).
+// Grid (1024-token blocks, scoring layers): one thread per (4 consecutive
+// tokens, layer), loading each query head's raw scores of its 4 tokens as one
+// 16-byte vector (page-major raw: a page's 128 scores of one head are
+// contiguous).  A CTA covers 8 pages; the request of each page and its
+// per-head mean, denominator and reciprocal for this layer are staged in
+// shared memory first.  The thread writes the layer's head-max row for its 4
+// tokens; aggregate_rows then reduces the layers (the same path serves TP=1
+// and the TP sync).
+constexpr int kNormPages = 8;  // pages per CTA (256 threads x 4 tokens)
+
 __global__ void __launch_bounds__(256) normalize_kernel(const float* __restrict__ raw, int L, int heads,
-                                                        int64_t tok_total, const float* __restrict__ mean,
+                                                        int total_pages, const float* __restrict__ mean,
                                                         const float* __restrict__ den,
                                                         const int32_t* __restrict__ tokens,
                                                         const int32_t* __restrict__ page_off, int R,
                                                         float* rows) {
-  extern __shared__ float st[];  // [2 requests][heads] mean, den, 1/den
+  extern __shared__ float st[];  // [kNormPages][heads] mean, den, 1/den
+  __shared__ int req_s[kNormPages];
+  __shared__ int64_t start_s[kNormPages];
+  __shared__ int ntok_s[kNormPages];
   const int l = blockIdx.y;
-  const int64_t first = (int64_t)blockIdx.x * blockDim.x;
-  const int r_lo = request_of_page(page_off, R, (int)(first >> 7));
-  const int64_t last = min64(first + blockDim.x, tok_total) - 1;
-  const int r_hi = request_of_page(page_off, R, (int)(last >> 7));
-  for (int i = threadIdx.x; i < 2 * heads; i += blockDim.x) {
-    const int rr = i < heads ? r_lo : r_hi;
-    const int64_t g = ((int64_t)l * R + rr) * heads + i % heads;
-    st[i] = __ldg(mean + g);
-    const float d = __ldg(den + g);
-    st[2 * heads + i] = d;
-    st[4 * heads + i] = __frcp_rn(d);
+  const int page0 = blockIdx.x * kNormPages;
+  if (threadIdx.x < kNormPages) {
+    const int p = page0 + threadIdx.x;
+    int r = 0;
+    if (p < total_pages) {
+      r = request_of_page(page_off, R, p);
+      start_s[threadIdx.x] = (int64_t)__ldg(page_off + r) * kBlock;
+      ntok_s[threadIdx.x] = __ldg(tokens + r);
+    }
+    req_s[threadIdx.x] = r;
   }
   __syncthreads();
-  const int64_t tok = first + threadIdx.x;
-  if (tok >= tok_total) return;
-  const int p = (int)(tok >> 7);
-  const int r = p == (int)(first >> 7) ? r_lo : r_hi;  // a 256-token block spans two pages
-  const int t = (int)(tok - (int64_t)__ldg(page_off + r) * kBlock);
-  float* out = rows + (int64_t)l * tok_total + tok;
-  if (t >= __ldg(tokens + r)) {  // page padding: keep rows finite for the MAX all-reduce
-    *out = 0.f;
+  float* mu_s = st;
+  float* dn_s = st + kNormPages * heads;
+  float* rc_s = st + 2 * kNormPages * heads;
+  for (int i = threadIdx.x; i < kNormPages * heads; i += blockDim.x) {
+    const int slot = i / heads;
+    if (page0 + slot >= total_pages) continue;
+    const int64_t g = ((int64_t)l * R + req_s[slot]) * heads + i % heads;
+    mu_s[i] = __ldg(mean + g);
+    const float d = __ldg(den + g);
+    dn_s[i] = d;
+    rc_s[i] = __frcp_rn(d);
+  }
+  __syncthreads();
+  const int slot = threadIdx.x >> 5;  // 32 threads x 4 tokens per page
+  const int p = page0 + slot;
+  if (p >= total_pages) return;
+  const int64_t tok_total = (int64_t)total_pages * kBlock;
+  const int64_t tok = (int64_t)p * kBlock + (threadIdx.x & 31) * 4;
+  const int t = (int)(tok - start_s[slot]);
+  const int n = ntok_s[slot];
+  float4* out = reinterpret_cast<float4*>(rows + (int64_t)l * tok_total + tok);
+  if (t >= n) {  // page padding: keep rows finite for the MAX sync
+    *out = make_float4(0.f, 0.f, 0.f, 0.f);
     return;
   }
-  const float* mu = st + (r == r_lo ? 0 : heads);
-  const float* dn = st + 2 * heads + (r == r_lo ? 0 : heads);
-  const float* rc = st + 4 * heads + (r == r_lo ? 0 : heads);
-  // page-major raw scores: the page's heads x 128 block is contiguous
-  const float* rl = raw + ((int64_t)l * (tok_total >> 7) + p) * heads * kBlock + (tok & (kBlock - 1));
-  constexpr int U = 16;  // independent loads in flight per thread
-  float z = -INFINITY;
+  const float* mu = mu_s + slot * heads;
+  const float* dn = dn_s + slot * heads;
+  const float* rc = rc_s + slot * heads;
+  const float4* rl = reinterpret_cast<const float4*>(raw + ((int64_t)l * total_pages + p) * heads * kBlock +
+                                                     (tok & (kBlock - 1)));
+  constexpr int U = 4;  // heads whose loads are in flight together (16 floats per thread)
+  float4 z = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
   for (int h0 = 0; h0 < heads; h0 += U) {
-    float x[U];
-#pragma unroll
-    for (int k = 0; k < U; ++k) x[k] = h0 + k < heads ? __ldg(rl + (int64_t)(h0 + k) * kBlock) : 0.f;
+    float4 x[U];
 #pragma unroll
     for (int k = 0; k < U; ++k)
-      if (h0 + k < heads) z = nan_max(z, div_by(x[k] - mu[h0 + k], dn[h0 + k], rc[h0 + k]));
+      if (h0 + k < heads) x[k] = __ldg(rl + (int64_t)(h0 + k) * (kBlock / 4));
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      const int h = h0 + k;
+      if (h < heads) {
+        const float m = mu[h], d = dn[h], c = rc[h];
+        z.x = nan_max(z.x, div_by(x[k].x - m, d, c));
+        z.y = nan_max(z.y, div_by(x[k].y - m, d, c));
+        z.z = nan_max(z.z, div_by(x[k].z - m, d, c));
+        z.w = nan_max(z.w, div_by(x[k].w - m, d, c));
+      }
+    }
   }
-  *out = z;
+  *out = make_float4(t + 0 < n ? z.x : 0.f, t + 1 < n ? z.y : 0.f, t + 2 < n ? z.z : 0.f, t + 3 < n ? z.w : 0.f);
 }
 
 __global__ void __launch_bounds__(256) aggregate_rows_kernel(const float* __restrict__ rows, int L,
@@ -667,12 +698,12 @@ extern "C" int kvc_normalize_aggregate(const float* raw, int L, int heads, int t
   KVC_CHECK_ARG(L > 0 && L <= 65535 && heads > 0 && R >= 0 && total_pages >= 0, KVC_EINVAL);
   KVC_CHECK_ARG(layer_aggregation == KVC_AGG_MEAN || layer_aggregation == KVC_AGG_MAX, KVC_EINVAL);
   if (R == 0 || total_pages == 0) return KVC_OK;
-  const int64_t tok_total = (int64_t)total_pages * kBlock;
-  const dim3 grid((unsigned)((tok_total + 255) / 256), (unsigned)L);
-  const size_t smem = (size_t)6 * heads * sizeof(float);
+  KVC_CHECK_ARG(aligned(raw, 16) && aligned(rows_out, 16), KVC_EALIGN);
+  const dim3 grid((unsigned)((total_pages + kNormPages - 1) / kNormPages), (unsigned)L);
+  const size_t smem = (size_t)3 * kNormPages * heads * sizeof(float);
   if (smem > 48 * 1024) return KVC_EUNSUPPORTED;
   cudaStream_t st = (cudaStream_t)stream;
-  normalize_kernel<<<grid, 256, smem, st>>>(raw, L, heads, tok_total, mean, denom, tokens, page_off, R, rows_out);
+  normalize_kernel<<<grid, 256, smem, st>>>(raw, L, heads, total_pages, mean, denom, tokens, page_off, R, rows_out);
   const int rc = launch_status();
   if (rc != KVC_OK || agg_out == nullptr) return rc;
   return kvc_aggregate_rows(rows_out, L, total_pages, tokens, page_off, R, layer_aggregation, agg_out, stream);
