@@ -306,3 +306,38 @@ def test_normalize_rows_equal_torch_fp32_bitwise(heads):
     nan = torch.isnan(ref)
     assert nan.any() and torch.equal(torch.isnan(rows), nan)
     assert torch.equal(rows[~nan].view(torch.int32), ref[~nan].view(torch.int32))
+
+
+@pytest.mark.parametrize("heads,parts", [(1, 4), (5, 4), (40, 4), (40, 1), (200, 4)])
+def test_head_stats_match_fp64_var_mean(heads, parts):
+    """kvc_head_stats from per-partial (sum, M2) equals torch.var_mean(correction=0) in fp64 within 1e-5."""
+    lib = N.lib()
+    lengths = [1, 129, 2049, 5000]
+    pages = [-(-t // 128) for t in lengths]
+    off = [0]
+    for p in pages:
+        off.append(off[-1] + p)
+    P, L, R, span = off[-1], 2, len(lengths), 128 // parts
+    g = torch.Generator().manual_seed(heads + parts)
+    raw = torch.randn(L, heads, P * 128, generator=g, dtype=torch.float64) * 3 + 50  # large mean, small spread
+    part = torch.zeros(L, P * parts, heads, 2, dtype=torch.float64)
+    ref_mean = torch.empty(L, R, heads, dtype=torch.float64)
+    ref_var = torch.empty(L, R, heads, dtype=torch.float64)
+    for r, t in enumerate(lengths):
+        x = raw[:, :, off[r] * 128: off[r] * 128 + t]
+        ref_var[:, r], ref_mean[:, r] = torch.var_mean(x, dim=-1, correction=0)
+        for q in range(-(-t // span)):
+            seg = x[:, :, q * span: min(t, (q + 1) * span)]
+            part[:, off[r] * parts + q, :, 0] = seg.sum(-1)
+            part[:, off[r] * parts + q, :, 1] = ((seg - seg.mean(-1, keepdim=True)) ** 2).sum(-1)
+    dev = lambda a, dt: a.to(dtype=dt).contiguous().cuda()
+    partial = dev(part, torch.float32)
+    out = [torch.empty(L * R * heads, device="cuda") for _ in range(3)]
+    assert lib.kvc_head_stats(partial.data_ptr(), L, R, P, parts, heads,
+                              dev(torch.tensor(lengths), torch.int32).data_ptr(),
+                              dev(torch.tensor(off), torch.int32).data_ptr(), *(o.data_ptr() for o in out),
+                              torch.cuda.current_stream().cuda_stream) == 0
+    mean, var, den = (o.cpu().double().view(L, R, heads) for o in out)
+    torch.testing.assert_close(mean, ref_mean, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(var, ref_var, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(den, ref_var.clamp_min(1e-6).sqrt(), rtol=1e-5, atol=1e-6)

@@ -370,51 +370,90 @@ __global__ void __launch_bounds__(kScoreWarps * 32) score_max_kernel(const __gri
 // per-head statistics
 // --------------------------------------------------------------------------
 
-struct Moments {
-  double n, mean, m2;
-};
-
-__device__ __forceinline__ Moments chan(Moments x, Moments y) {
-  if (y.n == 0) return x;
-  if (x.n == 0) return y;
-  const double n = x.n + y.n;
-  const double d = y.mean - x.mean;
-  return {n, x.mean + d * (y.n / n), x.m2 + y.m2 + d * d * (x.n * y.n / n)};
+// One CTA per (scoring layer, request).  The request's partials are the
+// contiguous range [p0*parts, p1*parts) x heads of float2 (partial sum, sum of
+// squared deviations from the partial's own mean).  Thread i owns head
+// i % heads and every (blockDim / heads)-th partial of it, so a warp's loads
+// are contiguous.  Two passes, both in fp64 and in a fixed order:
+//   mean = (sum of the partial sums) / T
+//   M2   = sum over partials of (M2_q + n_q * (mean_q - mean)^2)
+// (the exact decomposition of the sum of squares about the overall mean), then
+// var = M2 / T (population variance, as torch.var_mean(correction=0)).
+__device__ __forceinline__ double reduce_slots(double v, double* red, int heads, int slots) {
+  // sum of the `slots` per-thread values of each head, slot order fixed; returns it to slot 0 threads
+  red[threadIdx.x] = v;
+  __syncthreads();
+  double s = 0.0;
+  if (threadIdx.x < heads)
+    for (int j = 0; j < slots; ++j) s += red[j * heads + threadIdx.x];
+  __syncthreads();
+  return s;
 }
 
-__global__ void __launch_bounds__(256) head_stats_kernel(const float* __restrict__ partial, int L, int R,
-                                                         int total_pages, int parts, int heads,
-                                                         const int32_t* __restrict__ tokens,
-                                                         const int32_t* __restrict__ page_off,
-                                                         float* mean_out, float* var_out, float* den_out) {
+__global__ void __launch_bounds__(1024) head_stats_kernel(const float* __restrict__ partial, int L, int R,
+                                                          int total_pages, int parts, int heads,
+                                                          const int32_t* __restrict__ tokens,
+                                                          const int32_t* __restrict__ page_off,
+                                                          float* mean_out, float* var_out, float* den_out) {
+  extern __shared__ double red[];  // [blockDim]
+  __shared__ double mean_s[1024];
   const int l = blockIdx.x, r = blockIdx.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int p0 = page_off[r], p1 = page_off[r + 1], T = tokens[r];
   const int span = kBlock / parts;  // tokens per partial
   (void)L;
+  const int slots = blockDim.x / heads;  // threads per head
+  const int h = threadIdx.x % heads, j = threadIdx.x / heads;
+  const bool live = j < slots;
   const float2* part = reinterpret_cast<const float2*>(partial) + (int64_t)l * total_pages * parts * heads;
-  const int hg = blockIdx.z * (blockDim.x >> 5) + warp;  // one warp per query head
-  if (hg < heads) {
-    Moments m{0, 0, 0};
-    for (int q = p0 * parts + lane; q < p1 * parts; q += 32) {
-      const int n = min(span, T - (q - p0 * parts) * span);
-      if (n <= 0) continue;
-      const float2 v = part[(int64_t)q * heads + hg];
-      m = chan(m, Moments{(double)n, (double)v.x / n, (double)v.y});
-    }
+  const int q0 = p0 * parts;
+  const int q1 = min(p1 * parts, q0 + (T + span - 1) / span);  // padding partials hold nothing
+  constexpr int U = 8;  // partials whose loads are in flight together
+  // pass 1: sum of partial sums
+  double s = 0.0;
+  if (live) {
+    for (int q = q0 + j; q < q1; q += U * slots) {
+      float x[U];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      Moments y{__shfl_xor_sync(0xffffffffu, m.n, o), __shfl_xor_sync(0xffffffffu, m.mean, o),
-                __shfl_xor_sync(0xffffffffu, m.m2, o)};
-      m = chan(m, y);
+      for (int u = 0; u < U; ++u) {
+        const int qq = q + u * slots;
+        x[u] = qq < q1 ? __ldg(part + (int64_t)qq * heads + h).x : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) s += (double)x[u];
     }
-    if (lane == 0) {
-      const int64_t i = ((int64_t)l * R + r) * heads + hg;
-      const float var = m.n > 0 ? (float)(m.m2 / m.n) : NAN;
-      mean_out[i] = (float)m.mean;
-      var_out[i] = var;
-      den_out[i] = sqrtf(fmaxf(var, 1e-6f));
+  }
+  s = reduce_slots(live ? s : 0.0, red, heads, slots);
+  if (threadIdx.x < heads) mean_s[threadIdx.x] = T > 0 ? s / T : 0.0;
+  __syncthreads();
+  const double mu = mean_s[h];
+  // pass 2: sum of squares about the overall mean
+  double m2 = 0.0;
+  if (live) {
+    for (int q = q0 + j; q < q1; q += U * slots) {
+      float2 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int qq = q + u * slots;
+        v[u] = qq < q1 ? __ldg(part + (int64_t)qq * heads + h) : make_float2(0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int qq = q + u * slots;
+        if (qq < q1) {
+          const int n = min(span, T - (qq - q0) * span);
+          const double d = (double)v[u].x / n - mu;
+          m2 += (double)v[u].y + n * d * d;
+        }
+      }
     }
+  }
+  m2 = reduce_slots(live ? m2 : 0.0, red, heads, slots);
+  if (threadIdx.x < heads) {
+    const int64_t i = ((int64_t)l * R + r) * heads + threadIdx.x;
+    const float var = T > 0 ? (float)(m2 / T) : NAN;
+    mean_out[i] = T > 0 ? (float)mean_s[threadIdx.x] : NAN;
+    var_out[i] = var;
+    den_out[i] = sqrtf(fmaxf(var, 1e-6f));
   }
 }
 
@@ -685,7 +724,12 @@ extern "C" int kvc_head_stats(const float* partial, int L, int R, int total_page
   KVC_CHECK_ARG(L > 0 && R >= 0 && heads > 0 && total_pages >= 0, KVC_EINVAL);
   KVC_CHECK_ARG(parts_per_page == 1 || parts_per_page == 4, KVC_EINVAL);
   if (R == 0) return KVC_OK;
-  head_stats_kernel<<<dim3(L, R, (heads + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
+  KVC_CHECK_ARG(heads <= 1024, KVC_EUNSUPPORTED);
+  KVC_CHECK_ARG(R <= 65535, KVC_EINVAL);
+  // the largest whole number of threads per head that fits 1024 threads
+  const int threads = (1024 / heads) * heads;
+  const int block = std::min(1024, ((threads + 31) / 32) * 32);
+  head_stats_kernel<<<dim3(L, R), block, block * sizeof(double), (cudaStream_t)stream>>>(
       partial, L, R, total_pages, parts_per_page, heads, tokens, page_off, mean_out, var_out, denom_out);
   return launch_status();
 }
