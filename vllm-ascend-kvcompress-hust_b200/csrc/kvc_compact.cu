@@ -9,7 +9,7 @@
 // bases are not 16-byte aligned), two rows in flight per pass.  Rows under
 // 2 KB (few local heads under tensor parallelism) are copied as one flat
 // (row, vector) range per tile so each lane still has eight vectors in flight.
-#include "kvc_common.cuh"
+#include "kvc_async.cuh"
 
 namespace kvc {
 
@@ -174,6 +174,71 @@ __global__ void __launch_bounds__(kCopyThreads, SMALL ? 3 : 4) compact_kernel(co
   }
 }
 
+// Bulk-copy variant (16-byte aligned rows up to kBulkWarpBytes / 2): the TMA
+// engine moves whole rows.  One CTA per SM, kBulkWarps independent warps, each
+// owning kBulkWarpBytes of shared memory split into two row sets.  Per group of
+// up to 32 rows (one per lane): each lane bulk-loads its row into its slot of
+// the current set (completion counted on the set's mbarrier), the warp waits
+// for the set, then each lane bulk-stores its slot to the destination row and
+// commits a bulk group.  The next group uses the other set, so its loads fly
+// while the previous group's stores drain; a slot is reloaded only after the
+// lane's store from it two groups earlier has finished reading it.
+constexpr int kBulkWarps = 8;
+constexpr int kBulkWarpBytes = 24 * 1024;
+constexpr int kBulkSmem = kBulkWarps * kBulkWarpBytes;
+
+__global__ void __launch_bounds__(kBulkWarps * 32, 1) compact_bulk_kernel(const __grid_constant__ CompactArgs a) {
+  extern __shared__ __align__(128) uint8_t bulk_sm[];
+  __shared__ __align__(8) uint64_t bars[kBulkWarps][2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rb = (uint32_t)a.row_bytes;
+  const int gs = min(32, (int)(kBulkWarpBytes / rb) / 2);  // rows per group (host: >= 1)
+  const uint32_t buf = smem_u32(bulk_sm + warp * kBulkWarpBytes);
+  const uint32_t bar0 = smem_u32(&bars[warp][0]);
+  if (lane == 0) {
+    mbar_init(bar0, 1);
+    mbar_init(bar0 + 8, 1);
+    mbar_init_fence();
+  }
+  __syncwarp();
+  const int64_t rows = (int64_t)a.N * 2 * a.R * a.budget;
+  const int tr = a.tile_rows;
+  const int64_t tiles = (rows + tr - 1) / tr;
+  const int64_t nwarps = (int64_t)gridDim.x * kBulkWarps;
+  uint32_t parity = 0;  // bit s: phase parity of set s's barrier
+  int grp = 0;
+  bool ok = true;
+  for (int64_t tile = (int64_t)blockIdx.x * kBulkWarps + warp; ok && tile < tiles; tile += nwarps) {
+    const int64_t q = tile * tr + lane;
+    const char* my_src = nullptr;
+    char* my_dst = nullptr;
+    if (lane < tr && q < rows) resolve_row(a, q, my_src, my_dst);
+    const int nrows = (int)min64(tr, rows - tile * tr);
+    for (int k0 = 0; ok && k0 < nrows; k0 += gs, ++grp) {
+      const int set = grp & 1;
+      const int from = min(k0 + lane, 31);
+      const char* s = (const char*)__shfl_sync(0xffffffffu, (unsigned long long)my_src, from);
+      char* d = (char*)__shfl_sync(0xffffffffu, (unsigned long long)my_dst, from);
+      const bool mine = lane < min(gs, nrows - k0) && s != nullptr;
+      const unsigned mask = __ballot_sync(0xffffffffu, mine);
+      bulk_wait_read<1>();  // this lane's store from this set (two groups ago) has read its slot
+      if (mask) {
+        const uint32_t bar = bar0 + 8 * set;
+        const uint32_t slot = buf + (uint32_t)(set * gs + lane) * rb;
+        if (lane == 0) mbar_expect_tx(bar, (uint32_t)__popc(mask) * rb);
+        __syncwarp();
+        if (mine) bulk_load(slot, s, rb, bar);
+        ok = mbar_wait(bar, (parity >> set) & 1u, a.error_flag);
+        if (!ok) mbar_wait(bar, (parity >> set) & 1u, nullptr);  // let loads in flight land before exiting
+        parity ^= 1u << set;
+        if (ok && mine) bulk_store(d, slot, rb);
+      }
+      bulk_commit();  // one group per lane per round, empty or not, so wait_read<1> means "two rounds ago"
+    }
+  }
+  bulk_wait_all();
+}
+
 __global__ void stage_commit_kernel(const int64_t* __restrict__ dst_blocks, const int64_t* __restrict__ dst_block_off,
                                     int R, int64_t* staged_rows, int stride, int64_t* staged_offsets,
                                     const int64_t* __restrict__ semantic, int budget) {
@@ -261,6 +326,20 @@ int compact_blocks_per_sm() {
   return n;
 }
 
+// One-time opt-in to the bulk kernel's shared memory (per device, first call before any capture).
+bool bulk_ready() {
+  static int state[64] = {0};  // 0 unknown, 1 ready, -1 unavailable
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  if (state[dev] == 0)
+    state[dev] = cudaFuncSetAttribute(compact_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBulkSmem) ==
+                         cudaSuccess
+                     ? 1
+                     : -1;
+  if (state[dev] < 0) cudaGetLastError();
+  return state[dev] > 0;
+}
+
 template <int VEC, bool SMALL>
 void launch_compact(const CompactArgs& a, int64_t tiles, cudaStream_t st) {
   compact_kernel<VEC, SMALL><<<copy_grid(tiles, compact_blocks_per_sm<VEC, SMALL>()), kCopyThreads, 0, st>>>(a);
@@ -317,7 +396,13 @@ extern "C" int kvc_compact(const void* const* k_layers, const void* const* v_lay
     const int64_t nvec = row_bytes / vec;
     a.nvec_shift = (nvec & (nvec - 1)) == 0 ? __builtin_ctzll((unsigned long long)nvec) : -1;
     const int64_t tiles = (rows + a.tile_rows - 1) / a.tile_rows;
-    if (row_bytes < 2048) {
+    // bulk copies pay off for rows of 1 KB and more (per-copy overhead dominates below)
+    const bool bulk = vec >= 16 && row_bytes % 16 == 0 && row_bytes >= 1024 && row_bytes <= kBulkWarpBytes / 2 &&
+                      bulk_ready();
+    if (bulk) {
+      const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(sm_count(), (tiles + kBulkWarps - 1) / kBulkWarps));
+      compact_bulk_kernel<<<grid, kBulkWarps * 32, kBulkSmem, st>>>(a);
+    } else if (row_bytes < 2048) {
       switch (vec) {
         case 32: launch_compact<32, true>(a, tiles, st); break;
         case 16: launch_compact<16, true>(a, tiles, st); break;

@@ -27,7 +27,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
-#include "kvc_common.cuh"
+#include "kvc_async.cuh"
 
 namespace kvc {
 
@@ -36,7 +36,6 @@ constexpr int kTcThreads = (kTcConsumers + 1) * 32;
 constexpr int kMaxTcLayers = 64;
 constexpr int kBoxElems = 64;                   // 128-byte swizzle span of 16-bit elements
 constexpr int kBoxBytes = kBoxElems * 2 * kBlock;  // one box: 128 tokens x 64 elements = 16 KB
-constexpr uint64_t kWaitNs = 2000000000ull;     // bounded mbarrier waits (2 s)
 
 __host__ __device__ constexpr int frag_steps(int F, int P) { return 4 * (F / 16) + P / 16; }
 
@@ -156,59 +155,12 @@ __global__ void __launch_bounds__(256) prepare_frag_kernel(const __grid_constant
 // PTX helpers (mbarrier, TMA, ldmatrix, mma)
 // ---------------------------------------------------------------------------
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-// Wait until the phase with the given parity has completed, at most kWaitNs.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t* flag) {
-  uint64_t start = 0;
-  for (uint32_t it = 0;; ++it) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (ok) return true;
-    if (it == 0) start = global_ns();
-    else if ((it & 63) == 0 && global_ns() - start > kWaitNs) {
-      raise_flag(flag, KVC_DEV_TIMEOUT);
-      return false;
-    }
-  }
-}
-
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* map, int c0, int c1, int c2, int c3,
                                             uint32_t bar) {
   asm volatile(
       "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
       ::"r"(dst), "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
       : "memory");
-}
-
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-               ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
-               : "memory");
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
@@ -352,7 +304,7 @@ __global__ void __launch_bounds__(kTcThreads, TcGeom<F, P>::kMinBlocks) score_tc
     }
     mbar_init(wfull, 1);
     mbar_init(wfree, kTcConsumers);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_init_fence();
   }
   __syncthreads();
   const int heads = a.kvh * a.G;
