@@ -259,6 +259,19 @@ int kvc_calibration_accumulate_noalloc(const void* q, int dtype, int64_t n_token
                                        double* im_sum, double* abs_sum, double* pass_sum, void* stream);
 
 /*
+ * Undo "half"-style RoPE of query rows in place, for statistics gathered from
+ * post-RoPE queries (online calibration; no reference counterpart).  Row t sits
+ * at position first_position + t; with theta = fp32(position) * omega[f] the
+ * rotated pair (o1, o2) = (q[f], q[F+f]) of every head becomes
+ * (o1 cos + o2 sin, o2 cos - o1 sin), rounded back to the row's dtype.
+ * q [n_tokens][row_stride] BF16/FP16 with heads x head_dim leading elements;
+ * omega [rotary_dim / 2] fp32.
+ */
+int kvc_unrotate_queries(void* q, int dtype, int64_t n_tokens, int64_t row_stride, int heads,
+                         int head_dim, int rotary_dim, int64_t first_position, const float* omega,
+                         void* stream);
+
+/*
  * Physical decode positions: out[i] = positions[i] - offsets[request_indices[i]].
  * Replaces shift_positions (methods/triattention/kernels.py:35-47).
  * index_bytes: 4 (int32 request indices) or 8 (int64).

@@ -172,6 +172,55 @@ inline int calib_vec(int F, int P, int64_t row_stride, const void* q) {
 
 using namespace kvc;
 
+// Undo "half"-style (NeoX) RoPE in place: with theta = fp32(position) * omega_f
+// (the fp32 product the rotary cache is built from) the rotation was
+//   o1 = x1 cos - x2 sin,  o2 = x2 cos + x1 sin   (x1 = q[f], x2 = q[F + f]),
+// so x1 = o1 cos + o2 sin, x2 = o2 cos - o1 sin.  One thread per (token, f):
+// it forms the angle once and applies it to every head.
+template <class E>
+__global__ void unrotate_kernel(uint16_t* q, int64_t n_tok, int64_t row_stride, int heads, int D, int F,
+                                int64_t first_pos, const float* __restrict__ omega) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_tok * F) return;
+  const int64_t t = i / F;
+  const int f = (int)(i - t * F);
+  const float theta = __fmul_rn((float)(first_pos + t), __ldg(omega + f));
+  float sn, cs;
+  sincosf(theta, &sn, &cs);
+  uint16_t* row = q + t * row_stride;
+  for (int h = 0; h < heads; ++h) {
+    uint16_t* x = row + (int64_t)h * D;
+    const float o1 = unpack1(x[f], E{}), o2 = unpack1(x[F + f], E{});
+    const float x1 = fmaf(o2, sn, o1 * cs);
+    const float x2 = fmaf(-o1, sn, o2 * cs);
+    x[f] = pack1(x1, E{});
+    x[F + f] = pack1(x2, E{});
+  }
+}
+
+extern "C" int kvc_unrotate_queries(void* q, int dtype, int64_t n_tokens, int64_t row_stride, int heads,
+                                    int head_dim, int rotary_dim, int64_t first_position, const float* omega,
+                                    void* stream) {
+  KVC_CHECK_ARG(q && omega, KVC_ENULL);
+  KVC_CHECK_ARG(dtype == KVC_BF16 || dtype == KVC_FP16, KVC_EINVAL);
+  KVC_CHECK_ARG(n_tokens >= 0 && heads > 0 && head_dim > 0 && rotary_dim > 0 && rotary_dim % 2 == 0 &&
+                    rotary_dim <= head_dim && first_position >= 0 && row_stride >= (int64_t)heads * head_dim,
+                KVC_EINVAL);
+  KVC_CHECK_ARG(aligned(q, 2), KVC_EALIGN);
+  if (n_tokens == 0) return KVC_OK;
+  const int F = rotary_dim / 2;
+  const int64_t work = n_tokens * F;
+  const unsigned grid = (unsigned)((work + 255) / 256);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == KVC_BF16)
+    unrotate_kernel<Bf16><<<grid, 256, 0, st>>>((uint16_t*)q, n_tokens, row_stride, heads, head_dim, F,
+                                                 first_position, omega);
+  else
+    unrotate_kernel<Fp16><<<grid, 256, 0, st>>>((uint16_t*)q, n_tokens, row_stride, heads, head_dim, F,
+                                                 first_position, omega);
+  return launch_status();
+}
+
 extern "C" int64_t kvc_calibration_workspace_doubles(int64_t n_tokens, int heads, int head_dim, int rotary_dim) {
   if (n_tokens <= 0 || heads <= 0 || head_dim <= 0 || rotary_dim <= 0 || rotary_dim > head_dim) return 0;
   const int F = rotary_dim / 2, P = head_dim - rotary_dim;

@@ -53,6 +53,15 @@ __device__ __forceinline__ float unpack1(uint16_t v, Fp16) {
   return __half2float(*reinterpret_cast<__half*>(&v));
 }
 
+__device__ __forceinline__ uint16_t pack1(float x, Bf16) {
+  const __nv_bfloat16 b = __float2bfloat16_rn(x);
+  return *reinterpret_cast<const uint16_t*>(&b);
+}
+__device__ __forceinline__ uint16_t pack1(float x, Fp16) {
+  const __half h = __float2half_rn(x);
+  return *reinterpret_cast<const uint16_t*>(&h);
+}
+
 // Element j (0..7) of a 16-byte vector of 16-bit elements.
 template <int J, class E>
 __device__ __forceinline__ float elem8(const uint4& v, E e) {

@@ -5,6 +5,12 @@ Option names, defaults and error conditions follow the reference
 configuration accepted there is accepted here with the same meaning.
 ``score_chunk_size`` only bounded the reference's CPU temporaries; the CUDA
 path streams whole pages and validates but does not need it.
+
+Two options exist only here and are off by default: ``online_calibration_window``
+(trailing prefill query rows captured per request and scoring layer through the
+method API's query-observation hooks, 0 = off) and
+``online_calibration_min_tokens`` (rows a layer must have accumulated before its
+online statistics replace the artefact's for scoring).
 """
 
 from __future__ import annotations
@@ -26,6 +32,7 @@ _KNOWN = frozenset({
     "kv_budget", "recompute_window", "position_policy", "protected_prefix_window",
     "protected_recent_window", "position_segments", "score_aggregation", "layer_aggregation",
     "score_chunk_size", "score_layer_stride", "min_output_tokens_for_compression",
+    "online_calibration_window", "online_calibration_min_tokens",
 })
 
 
@@ -67,6 +74,8 @@ class TriAttentionConfig:
     score_chunk_size: int = 512
     score_layer_stride: int = 8
     min_output_tokens_for_compression: int = 0
+    online_calibration_window: int = 0
+    online_calibration_min_tokens: int = 16384
 
     @property
     def compression_threshold_tokens(self) -> int:
@@ -102,6 +111,8 @@ class TriAttentionConfig:
             score_chunk_size=require_int(options, "score_chunk_size", 512),
             score_layer_stride=require_int(options, "score_layer_stride", 8),
             min_output_tokens_for_compression=require_int(options, "min_output_tokens_for_compression", 0),
+            online_calibration_window=require_int(options, "online_calibration_window", 0),
+            online_calibration_min_tokens=require_int(options, "online_calibration_min_tokens", 16384),
         )
         cfg._validate()
         return cfg
@@ -125,5 +136,9 @@ class TriAttentionConfig:
             raise ValueError("method option 'score_layer_stride' must be positive")
         if self.min_output_tokens_for_compression < 0:
             raise ValueError("method option 'min_output_tokens_for_compression' must be non-negative")
+        if self.online_calibration_window < 0:
+            raise ValueError("method option 'online_calibration_window' must be non-negative")
+        if self.online_calibration_min_tokens <= 0:
+            raise ValueError("method option 'online_calibration_min_tokens' must be positive")
         if self.calibration_max_length < 128:
             raise ValueError("method option 'calibration_max_length' must be at least 128")

@@ -263,6 +263,18 @@ def calibration_accumulate(q: torch.Tensor, heads: int, head_dim: int, rotary_di
         "kvc_calibration_accumulate")
 
 
+def unrotate_queries(q: torch.Tensor, heads: int, head_dim: int, rotary_dim: int, first_position: int,
+                     omega: torch.Tensor) -> None:
+    """Undo half-style RoPE of ``q`` [n, >= heads*head_dim] (bf16/fp16, CUDA) in place."""
+    require_cuda(q, omega)
+    if q.ndim != 2 or q.stride(1) != 1:
+        raise RuntimeError("unrotate_queries takes [tokens, heads*head_dim] rows with unit inner stride")
+    _need(omega, torch.float32, "omega")
+    N.check(N.lib().kvc_unrotate_queries(q.data_ptr(), _dtype_code(q.dtype), q.shape[0], q.stride(0), heads,
+                                         head_dim, rotary_dim, int(first_position), omega.data_ptr(), _stream()),
+            "kvc_unrotate_queries")
+
+
 def shift_positions(positions: torch.Tensor, request_indices: torch.Tensor, request_offsets: torch.Tensor,
                     output: torch.Tensor, error_flag: torch.Tensor | None = None) -> torch.Tensor:
     """``output = positions - request_offsets[request_indices]`` (reference kernels.py:35-47)."""

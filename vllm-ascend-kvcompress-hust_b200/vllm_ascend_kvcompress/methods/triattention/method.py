@@ -38,6 +38,8 @@ from ..base import (
     LayerCache,
     MethodRuntimeSpec,
     ModelShape,
+    QueryBatchSpan,
+    QueryObservation,
 )
 from . import kernels as K
 from .config import TriAttentionConfig
@@ -193,6 +195,113 @@ class TriAttentionMethod(KVCompressionMethod):
             min_output_tokens_for_compression=self.config.min_output_tokens_for_compression,
         )
 
+    # ---- online calibration through the query-observation hooks (opt-in) ------
+
+    @property
+    def query_window_tokens(self) -> int:
+        """Trailing prefill query rows captured per request and scoring layer (0: online calibration off)."""
+        return self.config.online_calibration_window
+
+    @property
+    def query_layer_indices(self) -> tuple[int, ...] | None:
+        """The scoring layers (their statistics are the only ones scoring reads)."""
+        if not self.config.online_calibration_window:
+            return None
+        if self.layer_caches:
+            return self._scoring_model_layers
+        shape_layers = self.model_shape.full_attention_layer_indices
+        return tuple(shape_layers[:: self.config.score_layer_stride])
+
+    def capture_query(self, layer: LayerCache, query: torch.Tensor, spans: tuple[QueryBatchSpan, ...]) -> None:
+        """Keep the last ``online_calibration_window`` post-RoPE query rows of each span's request.
+
+        ``query`` is the attention input of one forward, [rows, local heads x head_dim]
+        (or [rows, heads, head_dim]); rows of later forwards of the same request
+        append to the earlier ones, and only the most recent window is kept.
+        """
+        W = self.config.online_calibration_window
+        slot = self._scoring_slot.get(layer.layer_index) if W else None
+        if slot is None:
+            return
+        width = self.local_kv_heads * self.group * self.head_dim
+        rows = query.reshape(query.shape[0], -1)
+        if rows.shape[1] != width or rows.dtype not in (torch.bfloat16, torch.float16):
+            raise RuntimeError(f"captured query rows must be bf16/fp16 [tokens, {width}] on the bound device")
+        for span in spans:
+            take = min(span.end - span.start, W)
+            if take <= 0:
+                continue
+            buf, fill = self._observation(span.request_id, rows.dtype)
+            have = fill[slot]
+            if have + take <= W:
+                buf[slot, have:have + take].copy_(rows[span.end - take:span.end])
+                fill[slot] = have + take
+            else:  # keep the newest W rows, oldest first
+                keep = W - take
+                if keep:
+                    buf[slot, :keep].copy_(buf[slot, have - keep:have].clone())
+                buf[slot, keep:W].copy_(rows[span.end - take:span.end])
+                fill[slot] = W
+
+    def complete_query_observation(self, observation: QueryObservation) -> None:
+        """Undo RoPE of the buffered rows (positions end at ``semantic_num_tokens``) and reduce them.
+
+        Once a layer has accumulated ``online_calibration_min_tokens`` rows, its
+        q_mean_real / q_mean_imag / q_abs_mean (and q_pass_mean) are replaced in
+        the scoring tensors by the online means, in place, before the next step.
+        """
+        entry = self._observations.pop(observation.request_id, None)
+        if entry is None:
+            return
+        buf, fill = entry
+        heads = self.local_kv_heads * self.group
+        for slot, n in enumerate(fill):
+            if n <= 0:
+                continue
+            rows = buf[slot, :n]
+            K.unrotate_queries(rows, heads, self.head_dim, self.rotary_dim,
+                               int(observation.semantic_num_tokens) - n, self.scoring_omega[slot])
+            acc = self._online_sums[slot]
+            acc.add(rows, heads, self.head_dim, self.rotary_dim)
+            if acc.count >= self.config.online_calibration_min_tokens:
+                self._publish_online_stats(slot, acc)
+        self._free_buffers.append(buf)
+
+    def discard_query_observation(self, request_id: str) -> None:
+        entry = self._observations.pop(request_id, None)
+        if entry is not None:
+            self._free_buffers.append(entry[0])
+
+    def _observation(self, request_id: str, dtype: torch.dtype):
+        entry = self._observations.get(request_id)
+        if entry is None:
+            L, W = self.scoring_layer_count, self.config.online_calibration_window
+            shape = (L, W, self.local_kv_heads * self.group * self.head_dim)
+            buf = next((b for b in self._free_buffers if b.dtype == dtype), None)
+            if buf is not None:
+                self._free_buffers.remove(buf)
+            else:
+                buf = torch.empty(shape, dtype=dtype, device=self.offsets.device)
+            entry = self._observations[request_id] = (buf, [0] * L)
+        return entry
+
+    def _publish_online_stats(self, slot: int, acc) -> None:
+        """Online means of one scoring layer -> its scoring tensors (same addresses)."""
+        kvh, G, F = self.local_kv_heads, self.group, self.num_freq
+        n = float(acc.count)
+        qr = (acc.real_sum / n).float().view(kvh, G, F)
+        qi = (acc.imag_sum / n).float().view(kvh, G, F)
+        qa = (acc.abs_sum / n).float().view(kvh, G, F)
+        self.scoring_q_real[slot].copy_(qr)
+        self.scoring_q_imag[slot].copy_(qi)
+        self.scoring_extra[slot].copy_(qa - torch.sqrt(qr.square() + qi.square() + 1e-8))
+        if self.pass_dim and acc.pass_sum is not None:
+            qp = (acc.pass_sum / n).float().view(kvh, G, self.pass_dim)
+            if self.scoring_q_pass is not None:
+                self.scoring_q_pass[slot].copy_(qp)
+            self.scoring_q_pass_t[slot].copy_(qp.transpose(-1, -2))
+        self.online_published[slot] = acc.count
+
     def compatibility_reasons(self, worker: Any) -> tuple[str, ...]:
         del worker
         return self.calibration.validate(self.model_shape)
@@ -225,6 +334,7 @@ class TriAttentionMethod(KVCompressionMethod):
         if len(targets) != len(self.model_shape.full_attention_layer_indices):
             raise RuntimeError("allocated full-attention layer count does not match calibration")
         bound, seen = [], set()
+        self._model_layer_of = {c.name: c.layer_index for c in targets}
         for c in targets:
             if c.layer_index not in stats:
                 raise RuntimeError(f"attention layer {c.name!r} resolves to invalid model layer index {c.layer_index}")
@@ -252,6 +362,7 @@ class TriAttentionMethod(KVCompressionMethod):
         self._strict = os.environ.get(_STRICT_ENV, "") == "1"
         self._last_shape = (0, 0, 0, 0)
         self._bind_step()
+        self._bind_online_calibration()
 
     def compress(self, request: CompressionRequest) -> CompressionResult:
         return self.compress_many((request,))[0]
@@ -325,6 +436,17 @@ class TriAttentionMethod(KVCompressionMethod):
 
         tp = get_tp_group()
         return tp.device_group, int(tp.rank_in_group)
+
+    def _bind_online_calibration(self) -> None:
+        from ...calibration import LayerAccumulator
+
+        scoring = self.layer_caches[:: self.config.score_layer_stride]
+        self._scoring_model_layers = tuple(self._model_layer_of[c.name] for c in scoring)
+        self._scoring_slot = {idx: i for i, idx in enumerate(self._scoring_model_layers)}
+        self._observations: dict[str, tuple[torch.Tensor, list[int]]] = {}
+        self._free_buffers: list[torch.Tensor] = []
+        self._online_sums = [LayerAccumulator() for _ in scoring]
+        self.online_published = [0] * len(scoring)
 
     def _bind_peer_exchange(self, device: torch.device):
         """Peer-memory score sync when the TP group is an NCCL group of GPUs that can reach each other."""
