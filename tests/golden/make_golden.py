@@ -30,7 +30,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-sys.path.insert(0, os.environ.get("KVC_REFERENCE_SRC", "/root/reference/src"))
+if not os.environ.get("KVC_REFERENCE_SRC"):
+    raise SystemExit("set KVC_REFERENCE_SRC to the reference checkout's src directory")
+sys.path.insert(0, os.environ["KVC_REFERENCE_SRC"])
 sys.path.insert(1, str(ROOT))
 
 import kvc_workloads as W  # noqa: E402
