@@ -100,8 +100,57 @@ __device__ __forceinline__ void resolve_row(const CompactArgs& a, int64_t q, con
   dst = base_d + db * a.block_stride + (j & 127) * a.row_bytes;
 }
 
+// resolve_row in three stages, so that a warp copying narrow rows can issue
+// the next tile's dependent index loads between its copy passes: begin loads
+// the keep index and the request's offsets, middle the two block ids, end
+// checks the ranges and forms the addresses (same checks and flags).
+struct RowFetch {
+  int64_t q;  // -1: no row
+  int64_t idx, soff, doff, sb, db;
+  int32_t ntok;
+};
+
+__device__ __forceinline__ void fetch_begin(const CompactArgs& a, int64_t q, RowFetch& f) {
+  f.q = q;
+  if (q < 0) return;
+  const int64_t j = q % a.budget;
+  const int r = (int)((q / a.budget) % a.R);
+  f.idx = __ldg(a.keep + (int64_t)r * a.budget + j);
+  f.ntok = __ldg(a.tokens + r);
+  f.soff = __ldg(a.src_block_off + r);
+  f.doff = __ldg(a.dst_block_off + r);
+}
+
+__device__ __forceinline__ void fetch_middle(const CompactArgs& a, RowFetch& f) {
+  if (f.q < 0) return;
+  const int64_t j = f.q % a.budget;
+  f.sb = (f.idx >= 0 && f.idx < f.ntok) ? __ldg(a.src_blocks + f.soff + (f.idx >> 7)) : -1;
+  f.db = __ldg(a.dst_blocks + f.doff + (j >> 7));
+}
+
+__device__ __forceinline__ void fetch_end(const CompactArgs& a, const RowFetch& f, const char*& src, char*& dst) {
+  src = nullptr;
+  dst = nullptr;
+  if (f.q < 0) return;
+  if (f.idx < 0 || f.idx >= f.ntok) {
+    raise_flag(a.error_flag, KVC_DEV_TOKEN_RANGE);
+    return;
+  }
+  if (f.sb < 0 || f.sb >= a.num_blocks || f.db < 0 || f.db >= a.num_blocks) {
+    raise_flag(a.error_flag, KVC_DEV_BLOCK_RANGE);
+    return;
+  }
+  const int64_t j = f.q % a.budget;
+  const int64_t t = f.q / a.budget / a.R;
+  const int kv = (int)(t & 1);
+  const int layer = (int)(t >> 1);
+  const char* base = reinterpret_cast<const char*>(kv ? a.v_layers[layer] : a.k_layers[layer]);
+  src = base + f.sb * a.block_stride + (f.idx & 127) * a.row_bytes;
+  dst = const_cast<char*>(base) + f.db * a.block_stride + (j & 127) * a.row_bytes;
+}
+
 template <int VEC, bool SMALL>
-__global__ void __launch_bounds__(kCopyThreads, SMALL ? 3 : 4) compact_kernel(const __grid_constant__ CompactArgs a) {
+__global__ void __launch_bounds__(kCopyThreads, SMALL ? 2 : 4) compact_kernel(const __grid_constant__ CompactArgs a) {
   using T = typename Vec<VEC>::T;
   const int lane = threadIdx.x & 31;
   const int64_t rows = (int64_t)a.N * 2 * a.R * a.budget;
@@ -110,18 +159,41 @@ __global__ void __launch_bounds__(kCopyThreads, SMALL ? 3 : 4) compact_kernel(co
   const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int nvec = (int)(a.row_bytes / VEC);
+  const char* next_src = nullptr;
+  char* next_dst = nullptr;
+  if constexpr (SMALL) {  // the first tile's rows; later tiles are resolved one tile ahead
+    RowFetch f;
+    const int64_t q = warp0 * tr + lane;
+    fetch_begin(a, (warp0 < tiles && lane < tr && q < rows) ? q : -1, f);
+    fetch_middle(a, f);
+    fetch_end(a, f, next_src, next_dst);
+  }
   for (int64_t tile = warp0; tile < tiles; tile += nwarps) {
     const int64_t q = tile * tr + lane;
     const char* my_src = nullptr;
     char* my_dst = nullptr;
-    if (lane < tr && q < rows) resolve_row(a, q, my_src, my_dst);
+    if constexpr (SMALL) {
+      my_src = next_src;
+      my_dst = next_dst;
+    } else {
+      if (lane < tr && q < rows) resolve_row(a, q, my_src, my_dst);
+    }
     const int nrows = (int)min64(tr, rows - tile * tr);
     if constexpr (SMALL) {
       // rows narrower than 2 KB: spread the tile's (row, vector) pairs over the
-      // lanes so that every lane keeps kSmallU vectors in flight
+      // lanes so that every lane keeps kSmallU vectors in flight; the next
+      // tile's index loads run between the copy passes
+      RowFetch nf;
+      const int64_t nq = (tile + nwarps) * tr + lane;
+      fetch_begin(a, (tile + nwarps < tiles && lane < tr && nq < rows) ? nq : -1, nf);
       constexpr int kSmallU = VEC == 32 ? 4 : 8;  // 128 (256) bytes in flight per lane
       const int total = nrows * nvec;
+      bool middle_done = false;
       for (int e0 = 0; e0 < total; e0 += 32 * kSmallU) {
+        if (e0 > 0 && !middle_done) {
+          fetch_middle(a, nf);
+          middle_done = true;
+        }
         T x[kSmallU];
         char* dd[kSmallU];
 #pragma unroll
@@ -141,6 +213,8 @@ __global__ void __launch_bounds__(kCopyThreads, SMALL ? 3 : 4) compact_kernel(co
         for (int u = 0; u < kSmallU; ++u)
           if (dd[u]) store_vec<VEC>(dd[u], x[u]);
       }
+      if (!middle_done) fetch_middle(a, nf);
+      fetch_end(a, nf, next_src, next_dst);
     } else {
     constexpr int kU = VEC == 32 ? 2 : 4;  // vectors per lane per row in one pass
     for (int k = 0; k < nrows; k += 2) {
