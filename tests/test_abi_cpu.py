@@ -122,3 +122,30 @@ def test_step_rejects_bad_stage_masks_without_launch():
     assert lib.kvc_triattention_run(ctypes.byref(st), 0, None, None) == -22
     assert lib.kvc_triattention_run(ctypes.byref(st), 32, None, None) == -22
     assert lib.kvc_triattention_run(ctypes.byref(st), N.STAGE_TABLES, None, None) == -14
+
+
+def test_exchange_ipc_and_unrotate_validate_on_the_host():
+    lib = N.lib()
+    fake = ctypes.c_void_p(0x1000)
+    assert lib.kvc_tp_exchange_flag_words(8) == 17 and lib.kvc_tp_exchange_flag_words(0) == 0
+    # exchange: NULL tables, rank outside the world, world above the maximum, epoch 0, bad aggregation
+    assert lib.kvc_tp_exchange_max(None, fake, fake, 2, 0, 1, 1, fake, fake, 1, 0, 1, None, None) == -14
+    assert lib.kvc_tp_exchange_max(fake, fake, fake, 2, 2, 1, 1, fake, fake, 1, 0, 1, None, None) == -22
+    assert lib.kvc_tp_exchange_max(fake, fake, fake, N.TP_MAX_WORLD + 1, 0, 1, 1, fake, fake, 1, 0, 1, None,
+                                   None) == -22
+    assert lib.kvc_tp_exchange_max(fake, fake, fake, 2, 0, 1, 1, fake, fake, 1, 0, 0, None, None) == -22
+    assert lib.kvc_tp_exchange_max(fake, fake, fake, 2, 0, 1, 1, fake, fake, 1, 5, 1, None, None) == -22
+    # IPC: NULL arguments are refused before any CUDA call
+    handle = (ctypes.c_char * N.IPC_HANDLE_BYTES)()
+    off = ctypes.c_int64()
+    assert lib.kvc_ipc_export(0, None, handle, ctypes.byref(off)) == -14
+    assert lib.kvc_ipc_open(0, None, ctypes.byref(ctypes.c_void_p())) == -14
+    assert lib.kvc_ipc_close(0, None) == -14
+    # un-rotation: NULL, unknown dtype, odd rotary dim, rotary dim above head dim, short rows
+    assert lib.kvc_unrotate_queries(None, 0, 4, 128, 1, 128, 128, 0, fake, None) == -14
+    assert lib.kvc_unrotate_queries(fake, 7, 4, 128, 1, 128, 128, 0, fake, None) == -22
+    assert lib.kvc_unrotate_queries(fake, 0, 4, 128, 1, 128, 63, 0, fake, None) == -22
+    assert lib.kvc_unrotate_queries(fake, 0, 4, 128, 1, 64, 128, 0, fake, None) == -22
+    assert lib.kvc_unrotate_queries(fake, 0, 4, 100, 1, 128, 128, 0, fake, None) == -22
+    # head statistics: more query heads than one CTA covers
+    assert lib.kvc_head_stats(fake, 1, 1, 1, 4, 1025, fake, fake, fake, fake, fake, None) == -95
