@@ -599,12 +599,14 @@ int launch_score(const ScoreArgs& a, int aggregation, cudaStream_t st) {
   const int grid = (int)min64(want, (int64_t)sm_count() * 16);
   if (aggregation == KVC_AGG_MEAN) {
     const size_t smem = (size_t)kScoreWarps * a.warp_floats * sizeof(float);
-    static size_t configured = 0;
-    if (smem > 48 * 1024 && smem > configured) {
+    static size_t configured[64] = {};  // per device (per-context attribute)
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return KVC_ECUDA;
+    if (smem > 48 * 1024 && smem > configured[dev]) {
       if (cudaFuncSetAttribute(score_mean_kernel<G, E>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem) != cudaSuccess)
         return KVC_ECUDA;
-      configured = smem;
+      configured[dev] = smem;
     }
     score_mean_kernel<G, E><<<grid, kScoreWarps * 32, smem, st>>>(a);
   } else {

@@ -500,12 +500,14 @@ template <int F, int P, class E>
 int launch_tc(const TcArgs& a, cudaStream_t st) {
   using Gm = TcGeom<F, P>;
   if (a.units == 0) return KVC_OK;
-  static bool configured = false;
-  if (!configured) {
+  static bool configured[64] = {};  // per device: the shared-memory opt-in is a per-context attribute
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return KVC_ECUDA;
+  if (!configured[dev]) {
     if (cudaFuncSetAttribute(score_tc_kernel<F, P, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, Gm::kSmem) !=
         cudaSuccess)
       return KVC_ECUDA;
-    configured = true;
+    configured[dev] = true;
   }
   const int64_t cap = (int64_t)sm_count() * Gm::kMinBlocks;
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cap, a.units));
