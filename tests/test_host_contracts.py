@@ -153,3 +153,19 @@ def test_external_method_registration():
 
     register_method("dummy-ext", lambda o, v, s: Dummy())
     assert isinstance(create_method("dummy-ext", {}, None, None), Dummy)
+
+
+def test_workspaces_grow_only_and_keep_addresses_until_growth():
+    import torch
+
+    from vllm_ascend_kvcompress.methods.triattention.method import _Workspaces
+
+    ws = _Workspaces(torch.device("cpu"))
+    p1 = ws.ptr("raw", 100, torch.float32)
+    assert ws.ptr("raw", 80, torch.float32) == p1  # smaller requests reuse the buffer
+    assert ws.get("raw", 50, torch.float32).data_ptr() == p1 and ws.get("raw", 50, torch.float32).numel() == 50
+    p2 = ws.ptr("raw", 1000, torch.float32)  # growth reallocates (callers re-read addresses every step)
+    assert ws.get("raw", 1000, torch.float32).data_ptr() == p2
+    assert ws.ptr("raw", 1100, torch.float32) == p2  # grown by 1.25x plus slack
+    assert ws.ptr("keep", 4, torch.int64) != p2
+    assert ws.get("keep", 4, torch.int64).dtype == torch.int64
