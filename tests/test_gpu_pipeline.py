@@ -272,6 +272,19 @@ EDGE_CASES = {
     "kvh3_d64": _edge("kvh3_d64", W.Geometry(2, 3, 6, 64, 64, 1e4),
                       W.Options(kv_budget=512, protected_prefix_window=16, protected_recent_window=64,
                                 score_layer_stride=1), [1500, 700, 2600], 27),
+    # the longest sequence max_model_len allows: phases at ~2^17 radians, position 65535
+    "max_len_64k": _edge("max_len_64k", W.Geometry(1, 2, 4, 128, 128, 1e6),
+                         W.Options(kv_budget=4096, protected_prefix_window=128, protected_recent_window=512,
+                                   score_layer_stride=1), [65536], 28),
+    # a layer count that the stride does not divide: scoring layers 0, 3, 6
+    "stride3_7layers": _edge("stride3_7layers", W.Geometry(7, 2, 4, 64, 64, 1e4),
+                             W.Options(kv_budget=512, protected_prefix_window=16, protected_recent_window=64,
+                                       score_layer_stride=3), [1300, 900, 2100], 29),
+    # forty requests in one step
+    "forty_requests": _edge("forty_requests", W.Geometry(1, 2, 8, 128, 128, 1e6),
+                            W.Options(kv_budget=1024, protected_prefix_window=0, protected_recent_window=128,
+                                      score_layer_stride=1),
+                            [1024 + (i * 977) % 2000 for i in range(40)], 30),
     # a ragged batch of many requests
     "ragged": _edge("ragged", W.Geometry(2, 8, 40, 128, 128, 1e6),
                     W.Options(kv_budget=640, protected_prefix_window=64, protected_recent_window=128,
