@@ -360,6 +360,30 @@ def test_fp16_cache_and_padded_block_stride(tmp_path):
         assert bool((pad == -7.0).all()), "padding between pages must stay untouched"
 
 
+def test_fp16_partial_rope_matches_oracle(tmp_path):
+    """FP16 caches with partial RoPE (head_dim 256, rotary 64, 8 query heads per KV head)."""
+    w = _edge("fp16_partial", W.Geometry(2, 1, 8, 256, 64, 1e7, model_type="qwen3_5_moe_text"),
+              W.Options(kv_budget=768, protected_prefix_window=128, protected_recent_window=128,
+                        score_layer_stride=1), [2100, 1500], 31, per=16)
+    cpu = [W.kv_pages(w, layer, dtype=torch.float16) for layer in range(w.geometry.num_layers)]
+    gpu = to_gpu(cpu)
+    m = bind(w, gpu, tmp_path)
+    assert m.use_tensor_scorer and m.kv_dtype == torch.float16
+    idx = w.compressed()
+    reqs = W.b200_requests(w, indices=idx)
+    keep = m.select_many(reqs).cpu()
+    agg = m.last_stats[3].cpu()
+    ref = oracle_select(w, cpu, idx)
+    offs = page_offsets(w, idx)
+    for row, i in enumerate(idx):
+        assert_scores_close(agg[offs[row]:offs[row] + w.lengths[i]], ref[i][0])
+        assert_selection(w, ref[i][0], ref[i][1], keep[row])
+    m.compress_many(reqs)
+    m.check_device_errors()
+    torch.cuda.synchronize()
+    assert_compaction(w, cpu, gpu, {i: keep[row] for row, i in enumerate(idx)})
+
+
 def test_device_range_errors_are_reported(tmp_path):
     w = W.config0()
     gpu = to_gpu(cpu_caches(w))
