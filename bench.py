@@ -218,7 +218,8 @@ def reference_arm(args) -> None:
     value, info = run_cpu_sample(w, seq, repeats=steps)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
-        "warmup": 1, "ms_per_step": info["seconds"] * 1e3, "higher_is_better": True, "scaling": "strong",
+        "warmup": 1, "ms_per_step": info["seconds"] * 1e3, "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) BF16 K/V, random calibration stats)",
         "config": config_dict(w, world, distinct_layers(args, w)),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": info["threads"], "kind": "port",
