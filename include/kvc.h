@@ -329,6 +329,16 @@ int kvc_ipc_close(int device, void* base);
 int kvc_can_access_peer(int device, int peer);
 
 /*
+ * Host helpers (no reference counterpart): record a cudaEvent_t on `stream`,
+ * and copy `bytes` between two addresses the CUDA runtime knows (pinned host
+ * or device memory, direction inferred) asynchronously on `stream`.  They let a
+ * binding stage a step's metadata and arm its error read-back without a
+ * framework round trip per call.
+ */
+int kvc_record_event(void* event, void* stream);
+int kvc_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
+
+/*
  * One compression step in a single call.
  *
  * No reference counterpart: the reference issues each device op from Python

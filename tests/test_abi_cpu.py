@@ -149,3 +149,12 @@ def test_exchange_ipc_and_unrotate_validate_on_the_host():
     assert lib.kvc_unrotate_queries(fake, 0, 4, 100, 1, 128, 128, 0, fake, None) == -22
     # head statistics: more query heads than one CTA covers
     assert lib.kvc_head_stats(fake, 1, 1, 1, 4, 1025, fake, fake, fake, fake, fake, None) == -95
+
+
+def test_host_helpers_validate_without_cuda_calls():
+    lib = N.lib()
+    fake = ctypes.c_void_p(0x1000)
+    assert lib.kvc_record_event(None, None) == -14
+    assert lib.kvc_copy_async(None, fake, 4, None) == -14
+    assert lib.kvc_copy_async(fake, fake, -1, None) == -22
+    assert lib.kvc_copy_async(fake, fake, 0, None) == 0  # nothing to copy, nothing launched

@@ -68,6 +68,8 @@ _SIGNATURES = {
     "kvc_ipc_close": (c_int, [c_int, _P]),
     "kvc_can_access_peer": (c_int, [c_int, c_int]),
     "kvc_unrotate_queries": (c_int, [_P, c_int, c_int64, c_int64, c_int, c_int, c_int, c_int64, _P, _P]),
+    "kvc_record_event": (c_int, [_P, _P]),
+    "kvc_copy_async": (c_int, [_P, _P, c_int64, _P]),
     "kvc_triattention_step_size": (c_int64, []),
     "kvc_triattention_run": (c_int, [_P, c_int, _P, _P]),
 }

@@ -117,17 +117,24 @@ class _MetadataStager:
         self.cap = 0
         self.i = 0
         self.host: list[torch.Tensor] = []
-        self.events: list[torch.cuda.Event | None] = []
+        self.events: list[torch.cuda.Event] = []
         self.dev: torch.Tensor | None = None
 
     def _grow(self, n: int) -> None:
         for ev in self.events:  # old host buffers may still feed a copy
-            if ev is not None:
-                ev.synchronize()
+            ev.synchronize()
         cap = max(n, 2 * self.cap, 256)
         self.host = [torch.empty(cap, dtype=torch.int64).pin_memory() for _ in range(self.slots)]
-        self.events = [None] * self.slots
+        self.host_np = [h.numpy() for h in self.host]
+        self.host_ptr = [h.data_ptr() for h in self.host]
+        self.events = []
+        for _ in range(self.slots):
+            ev = torch.cuda.Event()
+            ev.record()  # creates the event (complete once the stream reaches it)
+            self.events.append(ev)
+        self.event_handles = [ev.cuda_event for ev in self.events]
         self.dev = torch.empty(cap, dtype=torch.int64, device=self.device)
+        self.dev_ptr = self.dev.data_ptr()
         self.cap = cap
 
     def stage(self, i64: list[int], i32: list[int]) -> tuple[torch.Tensor, torch.Tensor]:
@@ -138,17 +145,13 @@ class _MetadataStager:
             self._grow(n)
         slot = self.i
         self.i = (self.i + 1) % self.slots
-        ev = self.events[slot]
-        if ev is not None:
-            ev.synchronize()
-        host = self.host[slot]
-        h = host.numpy()
+        self.events[slot].synchronize()  # the copy that last read this host buffer is done
+        h = self.host_np[slot]
         h[:n64] = i64
         h.view("int32")[2 * n64: 2 * n64 + len(i32)] = i32
-        self.dev[:n].copy_(host[:n], non_blocking=True)
-        if ev is None:
-            ev = self.events[slot] = torch.cuda.Event()
-        ev.record()
+        lib, stream = N.lib(), K._stream()
+        N.check(lib.kvc_copy_async(self.dev_ptr, self.host_ptr[slot], 8 * n, stream), "kvc_copy_async")
+        N.check(lib.kvc_record_event(self.event_handles[slot], stream), "kvc_record_event")
         return self.dev[:n64], self.dev.view(torch.int32)[2 * n64: 2 * n64 + len(i32)]
 
 
@@ -745,10 +748,14 @@ class TriAttentionMethod(KVCompressionMethod):
     # ---- device error reporting ---------------------------------------------
 
     def _arm_error_check(self) -> None:
-        self._err_host.copy_(self._err, non_blocking=True)
+        """Queue the error word's read-back and an event behind it (checked at the next call)."""
         if self._err_ev is None:
             self._err_ev = torch.cuda.Event()
-        self._err_ev.record()
+            self._err_ev.record()  # creates the event
+            self._err_ev_handle = self._err_ev.cuda_event
+        lib, stream = N.lib(), K._stream()
+        N.check(lib.kvc_copy_async(self._err_host.data_ptr(), self._err.data_ptr(), 4, stream), "kvc_copy_async")
+        N.check(lib.kvc_record_event(self._err_ev_handle, stream), "kvc_record_event")
         self._err_event = self._err_ev
 
     def _raise_pending_device_error(self) -> None:
