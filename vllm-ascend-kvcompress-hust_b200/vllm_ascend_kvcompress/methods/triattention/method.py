@@ -6,12 +6,14 @@ name, runtime spec, compatibility check, binding rules (target vs MTP layers,
 layer-index checks, TP head sharding of the statistics) and result.  The work
 differs in shape: a whole step's requests are processed by one launch per
 stage over a ragged, page-padded token space, instead of one torch op chain
-per request and per layer:
+per request and per layer, and the stages are issued by one call into the
+library (``kvc_triattention_run``):
 
-    prepare coefficients -> score every page of every scoring layer -> per-head
-    moments -> normalise + head max (+ layer mean/max, or per-layer rows that
-    one NCCL MAX all-reduce synchronises across TP ranks) -> segmented select
-    -> one compaction launch for all layers and requests.
+    gather block tables -> prepare coefficients -> score every page of every
+    scoring layer -> per-head moments -> normalise + head max into per-layer
+    rows -> layer mean/max (under tensor parallelism: the NVLink peer exchange
+    kernel, or one NCCL MAX all-reduce then the layer reduction) -> segmented
+    select -> one compaction launch for all layers and requests.
 
 ``compress(request)`` is ``compress_many((request,))``; ``compress_many`` is an
 optional batched extension a provider may probe for.  All launches go to the
