@@ -197,6 +197,59 @@ def test_block_tables_of_any_int_dtype_and_padding_give_the_same_step(tmp_path):
         assert torch.equal(v1.view(torch.int16), v2.view(torch.int16))
 
 
+def test_later_round_uses_semantic_length_for_phases(tmp_path):
+    """A request compressed before has semantic > physical tokens: phases use the semantic count."""
+    from dataclasses import replace
+
+    from oracle import triattention_oracle as O
+    from cases import oracle_options, oracle_stats
+
+    w = W.config0()
+    cpu = cpu_caches(w)
+    gpu = to_gpu(cpu)
+    m = bind(w, gpu, tmp_path)
+    idx = w.compressed()
+    extra = [7777, 20000, 123]
+    reqs = [replace(r, semantic_num_tokens=r.physical_num_tokens + e) for r, e in zip(W.b200_requests(w), extra)]
+    keep = m.select_many(reqs).cpu()
+    agg = m.last_stats[3].cpu()
+    offs = page_offsets(w, idx)
+    stats, opts = oracle_stats(w), oracle_options(w)
+    offsets = O.geometric_offsets(w.options.max_model_len)
+    for row, (i, e) in enumerate(zip(idx, extra)):
+        req = O.OracleRequest(semantic_num_tokens=w.lengths[i] + e, physical_num_tokens=w.lengths[i],
+                              src_blocks=torch.tensor(w.src_tables[i]), dst_blocks=torch.tensor(w.dst_tables[i]))
+        r_agg, r_keep = O.select_request([c[0] for c in cpu], stats, req, opts, offsets, 1)
+        assert_scores_close(agg[offs[row]:offs[row] + w.lengths[i]], r_agg)
+        assert_selection(w, r_agg, r_keep, keep[row])
+    m.compress_many(reqs, stage_commit=True)
+    m.check_device_errors()
+    assert m.staged_offsets.cpu().tolist() == [w.lengths[i] + e - w.options.kv_budget for i, e in zip(idx, extra)]
+
+
+def test_tp4_rows_max_equals_tp1_emulated(tmp_path):
+    """Four TP ranks on one GPU: the elementwise max of their rows reproduces TP=1's selection."""
+    w = EDGE_CASES["ragged"]
+    idx = [i for i, t in enumerate(w.lengths) if t >= w.options.kv_budget]
+    cpu = cpu_caches(w)
+    full = bind(w, to_gpu(cpu), tmp_path)
+    reqs = W.b200_requests(w, indices=idx)
+    keep1 = full.select_many(reqs).cpu()
+    per = w.geometry.num_kv_heads // 4
+    ranks, rows = [], []
+    for r in range(4):
+        shard = [(k[:, :, r * per:(r + 1) * per].contiguous().cuda(), v[:, :, r * per:(r + 1) * per].contiguous().cuda())
+                 for k, v in cpu]
+        m = bind(w, shard, tmp_path, tp_size=4, tp_rank=r)
+        m._tp_all_reduce_max = lambda x: rows.append(x.clone())
+        m.select_many(reqs)
+        ranks.append(m)
+    best = torch.stack(rows).amax(0)
+    for m in ranks:
+        m._tp_all_reduce_max = lambda x, b=best: x.copy_(b)
+        assert torch.equal(m.select_many(reqs).cpu(), keep1)
+
+
 def test_select_keep_indices_hook_matches_batch(tmp_path):
     w = W.config0()
     gpu = to_gpu(cpu_caches(w))
