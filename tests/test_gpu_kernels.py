@@ -341,3 +341,32 @@ def test_head_stats_match_fp64_var_mean(heads, parts):
     torch.testing.assert_close(mean, ref_mean, rtol=1e-5, atol=1e-6)
     torch.testing.assert_close(var, ref_var, rtol=1e-5, atol=1e-6)
     torch.testing.assert_close(den, ref_var.clamp_min(1e-6).sqrt(), rtol=1e-5, atol=1e-6)
+
+
+def test_compaction_over_more_layers_than_one_launch_holds():
+    """kvc_compact splits more than 512 layers into several launches with the same result."""
+    blocks, rb = 12, 128 * 2 * 64 * 2  # 2 KV heads x head_dim 64 x bf16
+    g = torch.Generator(device="cuda").manual_seed(9)
+    k = torch.randn(blocks, 128, 2, 64, generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn(blocks, 128, 2, 64, generator=g, device="cuda").to(torch.bfloat16)
+    T, budget = 700, 256
+    src = torch.tensor([3, 7, 1, 9, 0, 5], dtype=torch.int64, device="cuda")
+    dst = torch.tensor([10, 11], dtype=torch.int64, device="cuda")
+    keep = torch.sort(torch.randperm(T, generator=torch.Generator().manual_seed(2))[:budget]).values.cuda()
+    meta = torch.tensor([T, 0, -(-T // 128)], dtype=torch.int32, device="cuda")
+    i64 = torch.tensor([0, src.numel(), 0, dst.numel(), T, T], dtype=torch.int64, device="cuda")
+    plan = K.BatchPlan(1, -(-T // 128), meta[:1], meta[1:], src, i64[:2], dst, i64[2:4], i64[4:5], i64[5:6],
+                       (T,), dst.numel())
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    expect_k, expect_v = k.clone(), v.clone()
+    slots = (src[keep // 128] * 128 + keep % 128)
+    out = (dst[torch.arange(budget, device="cuda") // 128] * 128 + torch.arange(budget, device="cuda") % 128)
+    expect_k.view(-1, 2, 64)[out] = k.view(-1, 2, 64)[slots]
+    expect_v.view(-1, 2, 64)[out] = v.view(-1, 2, 64)[slots]
+    n = 520  # the same cache pair named 520 times: every layer writes the same rows
+    K.compact(N.pointer_array([k.data_ptr()] * n), N.pointer_array([v.data_ptr()] * n), k.stride(0) * 2, blocks,
+              rb // 128, plan, keep, budget, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(k.view(torch.int16), expect_k.view(torch.int16))
+    assert torch.equal(v.view(torch.int16), expect_v.view(torch.int16))
