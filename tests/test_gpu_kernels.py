@@ -370,3 +370,34 @@ def test_compaction_over_more_layers_than_one_launch_holds():
     assert int(err.item()) == 0
     assert torch.equal(k.view(torch.int16), expect_k.view(torch.int16))
     assert torch.equal(v.view(torch.int16), expect_v.view(torch.int16))
+
+
+@pytest.mark.parametrize("kvh,head_dim", [(4, 128), (8, 256), (24, 256), (1, 8)])
+def test_compaction_row_widths(kvh, head_dim):
+    """1 KB, 4 KB and 12 KB rows (bulk copies; 12 KB is the largest they take) and 16-byte rows."""
+    blocks = 10
+    g = torch.Generator(device="cuda").manual_seed(kvh * head_dim)
+    k = torch.randn(blocks, 128, kvh, head_dim, generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn(blocks, 128, kvh, head_dim, generator=g, device="cuda").to(torch.bfloat16)
+    T, budget = 600, 200
+    src = torch.tensor([4, 0, 7, 2, 9], dtype=torch.int64, device="cuda")
+    dst = torch.tensor([8, 6], dtype=torch.int64, device="cuda")
+    keep = torch.sort(torch.randperm(T, generator=torch.Generator().manual_seed(kvh))[:budget]).values.cuda()
+    meta = torch.tensor([T, 0, -(-T // 128)], dtype=torch.int32, device="cuda")
+    i64 = torch.tensor([0, src.numel(), 0, dst.numel(), T, T], dtype=torch.int64, device="cuda")
+    plan = K.BatchPlan(1, -(-T // 128), meta[:1], meta[1:], src, i64[:2], dst, i64[2:4], i64[4:5], i64[5:6],
+                       (T,), dst.numel())
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    expect_k, expect_v = k.clone(), v.clone()
+    slots = src[keep // 128] * 128 + keep % 128
+    j = torch.arange(budget, device="cuda")
+    out = dst[j // 128] * 128 + j % 128
+    expect_k.view(-1, kvh, head_dim)[out] = k.view(-1, kvh, head_dim)[slots]
+    expect_v.view(-1, kvh, head_dim)[out] = v.view(-1, kvh, head_dim)[slots]
+    row_bytes = kvh * head_dim * 2
+    K.compact(N.pointer_array([k.data_ptr()] * 3), N.pointer_array([v.data_ptr()] * 3), k.stride(0) * 2, blocks,
+              row_bytes, plan, keep, budget, err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(k.view(torch.int16), expect_k.view(torch.int16))
+    assert torch.equal(v.view(torch.int16), expect_v.view(torch.int16))
