@@ -158,3 +158,31 @@ def test_host_helpers_validate_without_cuda_calls():
     assert lib.kvc_copy_async(None, fake, 4, None) == -14
     assert lib.kvc_copy_async(fake, fake, -1, None) == -22
     assert lib.kvc_copy_async(fake, fake, 0, None) == 0  # nothing to copy, nothing launched
+
+
+def test_header_compiles_as_c_and_links(tmp_path):
+    """include/kvc.h is a C header: a C11 program includes it, links the library and agrees on the
+    step descriptor's size and the offset of its last field (ctypes mirror included)."""
+    import shutil
+    import subprocess
+
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    src = tmp_path / "t.c"
+    src.write_text(
+        "#include <stddef.h>\n#include <stdio.h>\n#include \"kvc.h\"\n"
+        "int main(void) {\n"
+        "  printf(\"%d %lld %zu\\n\", kvc_abi_version(), (long long)kvc_triattention_step_size(),\n"
+        "         offsetof(kvc_triattention_step, error_flag));\n"
+        "  return 0;\n}\n")
+    libdir = N.library_path().parent
+    exe = tmp_path / "t"
+    r = subprocess.run([gcc, "-std=c11", "-Wall", "-Werror", "-pedantic", f"-I{HEADER.parent}", str(src),
+                        f"-L{libdir}", "-lkvc_b200", f"-Wl,-rpath,{libdir}", "-o", str(exe)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()
+    assert int(out[0]) == N.ABI_VERSION
+    assert int(out[1]) == ctypes.sizeof(N.TriAttentionStep)
+    assert int(out[2]) == N.TriAttentionStep.error_flag.offset
