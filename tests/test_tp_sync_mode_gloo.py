@@ -54,3 +54,27 @@ def test_exchange_layout_is_aligned_and_ordered():
     flags, agg, rows, total = exchange_layout(8, 6, 1000, 17)
     assert flags == 0 and agg == 256 and rows == 256 + 4096 and total == rows + 24064
     assert all(x % 256 == 0 for x in (agg, rows, total))
+
+
+def test_exchange_buffers_grow_collectively_only_when_needed(monkeypatch):
+    """ensure() rebuilds (a collective) only for a new layer count or more tokens than it holds."""
+    sys.path.insert(0, str(ROOT / "vllm-ascend-kvcompress-hust_b200"))
+    import torch
+
+    from vllm_ascend_kvcompress.methods.triattention import tp_exchange as T
+
+    calls = []
+
+    def fake_rebuild(self, layers, cap):
+        calls.append((layers, cap))
+        self.layers, self.cap_tokens = layers, cap
+
+    monkeypatch.setattr(T.PeerScoreExchange, "_rebuild", fake_rebuild)
+    monkeypatch.setattr(T.N, "lib", lambda: type("L", (), {"kvc_tp_exchange_flag_words": staticmethod(lambda w: 2 * w + 1)})())
+    ex = T.PeerScoreExchange(None, 0, 2, torch.device("cpu"))
+    ex.ensure(6, 1000)
+    ex.ensure(6, 900)       # fits
+    ex.ensure(6, 1000)      # fits exactly
+    ex.ensure(6, 1001)      # grows by at least 1.5x
+    ex.ensure(5, 10)        # a new layer count always rebuilds
+    assert calls == [(6, 1000), (6, 1500), (5, 128)]
