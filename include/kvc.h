@@ -227,7 +227,13 @@ int kvc_scatter_slots(void* cache, int64_t block_stride_bytes, int block_size,
  * im = q[F + f], |.| = sqrt(re^2 + im^2), and per (head, pass dim) sums of
  * q[rotary_dim + p], accumulated (+=) into fp64 outputs.
  * Replaces _LayerAccumulator.add (calibration.py:95-131).
- * workspace: kvc_calibration_workspace_doubles(...) doubles.
+ * workspace: any size of at least 3 * heads * (rotary_dim/2 + head_dim -
+ * rotary_dim) doubles (one partial row); kvc_calibration_workspace_doubles()
+ * gives the size at which the launch runs at full parallelism on the current
+ * device (at most one wave of partial rows, never more than
+ * ceil(n_tokens / 512)).  A smaller workspace plans fewer, longer partial rows.
+ * The fp32 partials make the last bits of the sums depend on the row count,
+ * i.e. on the device and the workspace size; they stay within 1e-6 relative.
  */
 int64_t kvc_calibration_workspace_doubles(int64_t n_tokens, int heads, int head_dim,
                                           int rotary_dim);
@@ -237,21 +243,39 @@ int kvc_calibration_accumulate(const void* q, int dtype, int64_t n_tokens, int64
                                double* workspace, int64_t workspace_doubles, void* stream);
 
 /*
+ * The same reduction over post-RoPE ("half" style) query rows, undoing the
+ * rotation in fp32 registers before summing: row t sits at position
+ * first_position + t, theta = fp32(position) * omega[f], and the rotated pair
+ * (o1, o2) = (q[f], q[F+f]) of every head counts as
+ * (o1 cos + o2 sin, o2 cos - o1 sin).  No rounding back to 16 bits happens
+ * between the un-rotation and the sums.  omega [rotary_dim / 2] fp32 (device).
+ * No reference counterpart (online calibration from the attention inputs; the
+ * reference's stats builder hooks the pre-RoPE projections, calibration.py:197-360).
+ */
+int kvc_calibration_accumulate_post_rope(const void* q, int dtype, int64_t n_tokens, int64_t row_stride,
+                                         int heads, int head_dim, int rotary_dim, int64_t first_position,
+                                         const float* omega, double* re_sum, double* im_sum,
+                                         double* abs_sum, double* pass_sum, double* workspace,
+                                         int64_t workspace_doubles, void* stream);
+
+/*
  * Allocation-free calibration reduction.  No counterpart in the reference: it
  * is an addition of this library for callers that cannot provide device
  * memory -- a process whose GPU memory is already reserved (vLLM sizes the KV
  * cache to the whole memory budget, so a later cudaMalloc may fail) or a
  * foreign-language host that binds only this C ABI without a device allocator.
- * Same inputs, outputs and results as kvc_calibration_accumulate; the chunk
- * partials live in a library-owned static device array of
- * KVC_CALIB_STATIC_SCRATCH_DOUBLES doubles (8 MiB), which every GPU that loads
- * the library keeps until process exit.  Calls whose
- * kvc_calibration_workspace_doubles() exceeds that return KVC_ECAPACITY
- * without launching (about 69k tokens per call for 40 heads x head_dim 128).
- * The first call on each device looks up the array's device address
- * (cudaGetSymbolAddress); make that first call before any stream capture.
- * All calls on a device share the array: calls that overlap on the GPU race.
- * No cudaMalloc/cudaFree or other allocating routine is called.
+ * Same inputs, outputs and results (within 1e-6 relative) as
+ * kvc_calibration_accumulate; the partial rows live in a library-owned static
+ * device array of KVC_CALIB_STATIC_SCRATCH_DOUBLES doubles (8 MiB), which every
+ * GPU that loads the library keeps until process exit.  The launch plans only
+ * as many partial rows as the array holds, so any token count is served; a
+ * head geometry whose one partial row (3 * heads * (rotary_dim/2 + head_dim -
+ * rotary_dim) doubles) exceeds the array returns KVC_ECAPACITY without
+ * launching.  The first call on each device (and the first after that device's
+ * context is reset) looks up the array's device address with
+ * cudaGetSymbolAddress; make that first call before any stream capture.  All
+ * calls on a device share the array: calls that overlap on the GPU race.  No
+ * cudaMalloc/cudaFree or other allocating routine is called.
  */
 #define KVC_CALIB_STATIC_SCRATCH_DOUBLES (1 << 20)
 int kvc_calibration_accumulate_noalloc(const void* q, int dtype, int64_t n_tokens, int64_t row_stride,

@@ -3,10 +3,23 @@
 // Columns: a "rope unit" is (head, V consecutive frequencies) -- the thread
 // reads V real parts q[f..f+V) and the matching V imaginary parts
 // q[F+f..F+f+V) (16-byte vectors when V = 8) -- and a "pass unit" is (head, V
-// consecutive unrotated dims).  Each thread sums its column over a fixed chunk
-// of tokens in fp32 (|q| = sqrt(re^2 + im^2) per element) and writes the chunk
-// partial; a second kernel adds the chunk partials in a fixed order in fp64
-// into the caller's running fp64 sums (deterministic, atomics-free).
+// consecutive unrotated dims).  The tokens are split into `rows` equal
+// contiguous ranges (one per CTA row of the grid); each thread sums its column
+// over its range in fp32 (|q| = sqrt(re^2 + im^2) per element) and writes that
+// partial; a second kernel adds the partials in a fixed order in fp64 into the
+// caller's running fp64 sums (atomics-free).  `rows` is at most one wave of
+// resident CTAs and at most what the caller's workspace holds, so the fp32
+// rounding -- and with it the last bits of the result -- is deterministic for a
+// given device, workspace size and input, not across GPU models.
+//
+// Post-RoPE input (online calibration): the rotation of each row is undone in
+// fp32 registers right after the load (theta = fp32(position) * omega_f, the
+// product the rotary cache is built from), so the statistics see no extra
+// rounding to the cache's 16-bit type.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <climits>
 #include <mutex>
 
 #include "kvc_common.cuh"
@@ -21,7 +34,9 @@ struct CalibArgs {
   int64_t n_tok, row_stride;
   int H, D, F, P, V;
   int rope_cols, cols;
-  double* ws;  // [nchunk][cols][3V]
+  double* ws;            // [rows][cols][3V]
+  const float* omega;    // [F] for post-RoPE rows (positions first_pos + t), else null
+  int64_t first_pos;
 };
 
 // |q| of one frequency pair (hardware square root: within 2 ulp of the
@@ -46,7 +61,22 @@ __device__ __forceinline__ void load_vals(const uint16_t* p, float (&x)[V]) {
   }
 }
 
-template <int V, class E>
+// Undo "half"-style RoPE of V frequency pairs of token position `pos` in fp32:
+// the rotation was o1 = x1 cos - x2 sin, o2 = x2 cos + x1 sin.
+template <int V>
+__device__ __forceinline__ void unrotate_vals(float (&re)[V], float (&im)[V], const float* __restrict__ omega, int f,
+                                              int64_t pos) {
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    float sn, cs;
+    sincosf(__fmul_rn((float)pos, __ldg(omega + f + j)), &sn, &cs);
+    const float o1 = re[j], o2 = im[j];
+    re[j] = fmaf(o2, sn, o1 * cs);
+    im[j] = fmaf(-o1, sn, o2 * cs);
+  }
+}
+
+template <int V, class E, bool ROT>
 __global__ void __launch_bounds__(1024) calib_partial_kernel(const __grid_constant__ CalibArgs a) {
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
   if (col >= a.cols) return;
@@ -71,6 +101,10 @@ __global__ void __launch_bounds__(1024) calib_partial_kernel(const __grid_consta
         load_vals<V, E>(base + (t + u) * a.row_stride, xr[u]);
         load_vals<V, E>(base + (t + u) * a.row_stride + a.F, xi[u]);
       }
+      if constexpr (ROT) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) unrotate_vals<V>(xr[u], xi[u], a.omega, f, a.first_pos + t + u);
+      }
 #pragma unroll
       for (int u = 0; u < U; ++u)
 #pragma unroll
@@ -84,6 +118,7 @@ __global__ void __launch_bounds__(1024) calib_partial_kernel(const __grid_consta
       float xr[V], xi[V];
       load_vals<V, E>(base + t * a.row_stride, xr);
       load_vals<V, E>(base + t * a.row_stride + a.F, xi);
+      if constexpr (ROT) unrotate_vals<V>(xr, xi, a.omega, f, a.first_pos + t);
 #pragma unroll
       for (int j = 0; j < V; ++j) {
         re[j] += xr[j];
@@ -221,31 +256,47 @@ extern "C" int kvc_unrotate_queries(void* q, int dtype, int64_t n_tokens, int64_
   return launch_status();
 }
 
-extern "C" int64_t kvc_calibration_workspace_doubles(int64_t n_tokens, int heads, int head_dim, int rotary_dim) {
-  if (n_tokens <= 0 || heads <= 0 || head_dim <= 0 || rotary_dim <= 0 || rotary_dim > head_dim) return 0;
-  const int F = rotary_dim / 2, P = head_dim - rotary_dim;
-  // upper bound over vector widths: one column per element at V = 1
-  const int64_t cols_v1 = (int64_t)heads * (F + P);
-  const int64_t nchunk = (n_tokens + kCalibChunk - 1) / kCalibChunk;
-  return nchunk * cols_v1 * 3;
+namespace kvc {
+
+// Doubles of one partial row: every column writes 3V doubles (re, im, |.| or
+// V pass sums), i.e. 3 * heads * (F + P) whatever the vector width V.
+inline int64_t calib_row_doubles(int H, int F, int P) { return 3LL * H * (F + P); }
+
+struct CalibPlan {
+  int V, rope_cols, cols, threads, gx;
+  int64_t rows;  // partial rows = CTA rows of the grid
+};
+
+// Launch shape for n tokens at vector width V: one CTA spans all columns of a
+// token range where possible; the rows are at most ceil(n / kCalibChunk) and at
+// most one full wave of resident CTAs (no tail wave), and at most `max_rows`.
+inline CalibPlan calib_plan(int64_t n, int H, int F, int P, int V, int64_t max_rows) {
+  CalibPlan c{};
+  c.V = V;
+  c.rope_cols = H * (F / V);
+  c.cols = c.rope_cols + H * (P / V);
+  c.threads = std::min(1024, (c.cols + 31) / 32 * 32);
+  c.gx = (c.cols + c.threads - 1) / c.threads;
+  int per_sm = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, calib_partial_kernel<8, Bf16, false>, c.threads, 0) !=
+          cudaSuccess || per_sm < 1) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
+  const int64_t wave = std::max<int64_t>(1, (int64_t)sm_count() * per_sm / c.gx);
+  c.rows = std::min<int64_t>({(n + kCalibChunk - 1) / kCalibChunk, wave, max_rows, 65535});
+  c.rows = std::max<int64_t>(c.rows, 1);
+  return c;
 }
 
-extern "C" int kvc_calibration_accumulate(const void* q, int dtype, int64_t n_tokens, int64_t row_stride, int heads,
-                                          int head_dim, int rotary_dim, double* re_sum, double* im_sum,
-                                          double* abs_sum, double* pass_sum, double* workspace,
-                                          int64_t workspace_doubles, void* stream) {
-  KVC_CHECK_ARG(q && re_sum && im_sum && abs_sum && workspace, KVC_ENULL);
-  KVC_CHECK_ARG(dtype == KVC_BF16 || dtype == KVC_FP16, KVC_EINVAL);
-  KVC_CHECK_ARG(n_tokens >= 0 && heads > 0 && head_dim > 0 && rotary_dim > 0 && rotary_dim <= head_dim &&
-                    rotary_dim % 2 == 0 && row_stride >= (int64_t)heads * head_dim,
-                KVC_EINVAL);
+// Shared body of the calibration entry points (arguments validated by the caller).
+int calib_launch(const void* q, int dtype, int64_t n_tokens, int64_t row_stride, int heads, int head_dim,
+                 int rotary_dim, double* re_sum, double* im_sum, double* abs_sum, double* pass_sum, double* ws,
+                 int64_t ws_doubles, const float* omega, int64_t first_pos, cudaStream_t st) {
   const int F = rotary_dim / 2, P = head_dim - rotary_dim;
-  KVC_CHECK_ARG(P == 0 || pass_sum != nullptr, KVC_ENULL);
-  KVC_CHECK_ARG(aligned(q, 2), KVC_EALIGN);
-  if (n_tokens == 0) return KVC_OK;
-  KVC_CHECK_ARG(workspace_doubles >= kvc_calibration_workspace_doubles(n_tokens, heads, head_dim, rotary_dim),
-                KVC_EINVAL);
-  const int V = calib_vec(F, P, row_stride, q);
+  const int64_t max_rows = ws_doubles / calib_row_doubles(heads, F, P);
+  KVC_CHECK_ARG(max_rows >= 1, KVC_EINVAL);
+  const CalibPlan c = calib_plan(n_tokens, heads, F, P, calib_vec(F, P, row_stride, q), max_rows);
   CalibArgs a{};
   a.q = (const uint16_t*)q;
   a.n_tok = n_tokens;
@@ -254,37 +305,82 @@ extern "C" int kvc_calibration_accumulate(const void* q, int dtype, int64_t n_to
   a.D = head_dim;
   a.F = F;
   a.P = P;
-  a.V = V;
-  a.rope_cols = heads * (F / V);
-  a.cols = a.rope_cols + heads * (P / V);
-  a.ws = workspace;
-  int64_t nchunk = (n_tokens + kCalibChunk - 1) / kCalibChunk;  // upper bound of the partial rows
-  // one CTA spans all columns of a token range where possible; the ranges are
-  // sized so that the grid is one full wave of resident CTAs (no tail wave)
-  const int threads = std::min(1024, (a.cols + 31) / 32 * 32);
-  const int gx = (a.cols + threads - 1) / threads;
-  int per_sm = 1;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, calib_partial_kernel<8, Bf16>, threads, 0) !=
-          cudaSuccess || per_sm < 1)
-    per_sm = 1;
-  const int64_t wave = std::max<int64_t>(1, (int64_t)sm_count() * per_sm / gx);
-  nchunk = std::min<int64_t>(nchunk, wave);
-  KVC_CHECK_ARG(nchunk <= 65535, KVC_EINVAL);
-  const dim3 grid(gx, (unsigned)nchunk);
-  cudaStream_t st = (cudaStream_t)stream;
-#define KVC_CALIB(VV, EE) calib_partial_kernel<VV, EE><<<grid, threads, 0, st>>>(a)
+  a.V = c.V;
+  a.rope_cols = c.rope_cols;
+  a.cols = c.cols;
+  a.ws = ws;
+  a.omega = omega;
+  a.first_pos = first_pos;
+  const dim3 grid(c.gx, (unsigned)c.rows);
+#define KVC_CALIB(VV, EE)                                                                  \
+  (omega ? calib_partial_kernel<VV, EE, true><<<grid, c.threads, 0, st>>>(a)               \
+         : calib_partial_kernel<VV, EE, false><<<grid, c.threads, 0, st>>>(a))
   if (dtype == KVC_BF16) {
-    if (V == 8) KVC_CALIB(8, Bf16); else if (V == 2) KVC_CALIB(2, Bf16); else KVC_CALIB(1, Bf16);
+    if (c.V == 8) KVC_CALIB(8, Bf16); else if (c.V == 2) KVC_CALIB(2, Bf16); else KVC_CALIB(1, Bf16);
   } else {
-    if (V == 8) KVC_CALIB(8, Fp16); else if (V == 2) KVC_CALIB(2, Fp16); else KVC_CALIB(1, Fp16);
+    if (c.V == 8) KVC_CALIB(8, Fp16); else if (c.V == 2) KVC_CALIB(2, Fp16); else KVC_CALIB(1, Fp16);
   }
 #undef KVC_CALIB
   int rc = launch_status();
   if (rc != KVC_OK) return rc;
   const int64_t total = 3LL * heads * F + (int64_t)heads * P;
   calib_finalize_kernel<<<(unsigned)((total * 32 + 255) / 256), 256, 0, st>>>(
-      workspace, nchunk, a.cols, a.rope_cols, heads, F, P, V, re_sum, im_sum, abs_sum, pass_sum);
+      ws, c.rows, c.cols, c.rope_cols, heads, F, P, c.V, re_sum, im_sum, abs_sum, pass_sum);
   return launch_status();
+}
+
+inline int calib_check(const void* q, int dtype, int64_t n_tokens, int64_t row_stride, int heads, int head_dim,
+                       int rotary_dim, const double* re_sum, const double* im_sum, const double* abs_sum,
+                       const double* pass_sum) {
+  KVC_CHECK_ARG(q && re_sum && im_sum && abs_sum, KVC_ENULL);
+  KVC_CHECK_ARG(dtype == KVC_BF16 || dtype == KVC_FP16, KVC_EINVAL);
+  KVC_CHECK_ARG(n_tokens >= 0 && heads > 0 && head_dim > 0 && rotary_dim > 0 && rotary_dim <= head_dim &&
+                    rotary_dim % 2 == 0 && row_stride >= (int64_t)heads * head_dim,
+                KVC_EINVAL);
+  KVC_CHECK_ARG(rotary_dim == head_dim || pass_sum != nullptr, KVC_ENULL);
+  KVC_CHECK_ARG(aligned(q, 2), KVC_EALIGN);
+  return KVC_OK;
+}
+
+}  // namespace kvc
+
+extern "C" int64_t kvc_calibration_workspace_doubles(int64_t n_tokens, int heads, int head_dim, int rotary_dim) {
+  if (n_tokens <= 0 || heads <= 0 || head_dim <= 0 || rotary_dim <= 0 || rotary_dim > head_dim) return 0;
+  const int F = rotary_dim / 2, P = head_dim - rotary_dim;
+  // the largest row count any vector width can plan (the width depends on the
+  // caller's pointer and stride alignment)
+  int64_t rows = 1;
+  for (int V : {1, 2, 8})
+    if (F % V == 0 && P % V == 0) rows = std::max(rows, calib_plan(n_tokens, heads, F, P, V, INT64_MAX).rows);
+  return rows * calib_row_doubles(heads, F, P);
+}
+
+extern "C" int kvc_calibration_accumulate(const void* q, int dtype, int64_t n_tokens, int64_t row_stride, int heads,
+                                          int head_dim, int rotary_dim, double* re_sum, double* im_sum,
+                                          double* abs_sum, double* pass_sum, double* workspace,
+                                          int64_t workspace_doubles, void* stream) {
+  const int rc = calib_check(q, dtype, n_tokens, row_stride, heads, head_dim, rotary_dim, re_sum, im_sum, abs_sum,
+                             pass_sum);
+  if (rc != KVC_OK) return rc;
+  KVC_CHECK_ARG(workspace, KVC_ENULL);
+  if (n_tokens == 0) return KVC_OK;
+  return calib_launch(q, dtype, n_tokens, row_stride, heads, head_dim, rotary_dim, re_sum, im_sum, abs_sum, pass_sum,
+                      workspace, workspace_doubles, nullptr, 0, (cudaStream_t)stream);
+}
+
+extern "C" int kvc_calibration_accumulate_post_rope(const void* q, int dtype, int64_t n_tokens, int64_t row_stride,
+                                                    int heads, int head_dim, int rotary_dim, int64_t first_position,
+                                                    const float* omega, double* re_sum, double* im_sum,
+                                                    double* abs_sum, double* pass_sum, double* workspace,
+                                                    int64_t workspace_doubles, void* stream) {
+  const int rc = calib_check(q, dtype, n_tokens, row_stride, heads, head_dim, rotary_dim, re_sum, im_sum, abs_sum,
+                             pass_sum);
+  if (rc != KVC_OK) return rc;
+  KVC_CHECK_ARG(workspace && omega, KVC_ENULL);
+  KVC_CHECK_ARG(first_position >= 0, KVC_EINVAL);
+  if (n_tokens == 0) return KVC_OK;
+  return calib_launch(q, dtype, n_tokens, row_stride, heads, head_dim, rotary_dim, re_sum, im_sum, abs_sum, pass_sum,
+                      workspace, workspace_doubles, omega, first_position, (cudaStream_t)stream);
 }
 
 namespace kvc {
@@ -296,12 +392,15 @@ namespace kvc {
 // Some hosts cannot hand this library a device workspace: a process whose GPU
 // memory was reserved up front (vLLM sizes the KV cache to fill the memory
 // budget, so a later cudaMalloc can fail), or a foreign-language host that binds
-// only this C ABI and has no device allocator.  For them the chunk partials of
+// only this C ABI and has no device allocator.  For them the partial rows of
 // the calibration reduction live in one file-scope __device__ array that every
-// GPU loading the library keeps until process exit.  The array is shared by all
-// calls on a device: calls that overlap on the GPU (different streams or
-// threads without ordering) race on it.  Nothing in it must start at zero:
-// each call writes every partial it later reads.
+// GPU loading the library keeps until process exit.  The launch plans only as
+// many partial rows as the array holds (each thread then sums a longer token
+// range), so the token count is not limited; only a head geometry whose single
+// row exceeds the array is refused.  The array is shared by all calls on a
+// device: calls that overlap on the GPU (different streams or threads without
+// ordering) race on it.  Nothing in it must start at zero: each call writes
+// every partial it later reads.
 
 static __device__ __align__(256) double g_calib_scratch[KVC_CALIB_STATIC_SCRATCH_DOUBLES];
 
@@ -309,18 +408,48 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 
-// Device address of g_calib_scratch on the current device, resolved once per
-// device (host code must not use the symbol's name as a device pointer).
+PFN_cuCtxGetCurrent_v4000 ctx_current_fn() {
+  static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+  }
+  return fn;
+}
+
+// Device address of g_calib_scratch on the current device (host code must not
+// use the symbol's name as a device pointer).  Resolved on the first call per
+// device and again whenever the device's current context changes (a
+// cudaDeviceReset reloads the module, so an address cached before it would be
+// stale).
 int static_scratch(double** out) {
   static std::mutex mu;
   static double* ptrs[kMaxDevices] = {};
+  static CUcontext ctxs[kMaxDevices] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return KVC_ECUDA;
   std::lock_guard<std::mutex> lock(mu);
+  CUcontext ctx = nullptr;
+  if (ptrs[dev] != nullptr) {
+    PFN_cuCtxGetCurrent_v4000 cur = ctx_current_fn();
+    if (cur == nullptr || cur(&ctx) != CUDA_SUCCESS || ctx != ctxs[dev]) ptrs[dev] = nullptr;
+  }
   if (ptrs[dev] == nullptr) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_calib_scratch) != cudaSuccess || p == nullptr) return KVC_ECUDA;
+    if (cudaGetSymbolAddress(&p, g_calib_scratch) != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return KVC_ECUDA;
+    }
+    PFN_cuCtxGetCurrent_v4000 cur = ctx_current_fn();
+    ctx = nullptr;
+    if (cur != nullptr) cur(&ctx);
     ptrs[dev] = static_cast<double*>(p);
+    ctxs[dev] = ctx;
   }
   *out = ptrs[dev];
   return KVC_OK;
@@ -332,11 +461,15 @@ int static_scratch(double** out) {
 extern "C" int kvc_calibration_accumulate_noalloc(const void* q, int dtype, int64_t n_tokens, int64_t row_stride,
                                                   int heads, int head_dim, int rotary_dim, double* re_sum,
                                                   double* im_sum, double* abs_sum, double* pass_sum, void* stream) {
-  const int64_t need = kvc_calibration_workspace_doubles(n_tokens, heads, head_dim, rotary_dim);
-  if (need > KVC_CALIB_STATIC_SCRATCH_DOUBLES) return KVC_ECAPACITY;
-  double* scratch = nullptr;
-  const int rc = kvc::static_scratch(&scratch);
+  int rc = calib_check(q, dtype, n_tokens, row_stride, heads, head_dim, rotary_dim, re_sum, im_sum, abs_sum,
+                       pass_sum);
   if (rc != KVC_OK) return rc;
-  return kvc_calibration_accumulate(q, dtype, n_tokens, row_stride, heads, head_dim, rotary_dim, re_sum, im_sum,
-                                    abs_sum, pass_sum, scratch, KVC_CALIB_STATIC_SCRATCH_DOUBLES, stream);
+  const int F = rotary_dim / 2, P = head_dim - rotary_dim;
+  if (calib_row_doubles(heads, F, P) > KVC_CALIB_STATIC_SCRATCH_DOUBLES) return KVC_ECAPACITY;
+  if (n_tokens == 0) return KVC_OK;
+  double* scratch = nullptr;
+  rc = kvc::static_scratch(&scratch);
+  if (rc != KVC_OK) return rc;
+  return calib_launch(q, dtype, n_tokens, row_stride, heads, head_dim, rotary_dim, re_sum, im_sum, abs_sum, pass_sum,
+                      scratch, KVC_CALIB_STATIC_SCRATCH_DOUBLES, nullptr, 0, (cudaStream_t)stream);
 }

@@ -302,7 +302,10 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1) compact_bulk_kernel(const 
         if (lane == 0) mbar_expect_tx(bar, (uint32_t)__popc(mask) * rb);
         __syncwarp();
         if (mine) bulk_load(slot, s, rb, bar);
-        ok = mbar_wait(bar, (parity >> set) & 1u, a.error_flag);
+        // one verdict for the whole warp: a lane that saw the phase complete and a
+        // lane whose bound expired must leave (or go on) together, since the
+        // next group's shuffles and ballot name every lane
+        ok = __all_sync(0xffffffffu, mbar_wait(bar, (parity >> set) & 1u, a.error_flag));
         if (!ok) mbar_wait(bar, (parity >> set) & 1u, nullptr);  // let loads in flight land before exiting
         parity ^= 1u << set;
         if (ok && mine) bulk_store(d, slot, rb);

@@ -381,13 +381,15 @@ __global__ void __launch_bounds__(kTcThreads, TcGeom<F, P>::kMinBlocks) score_tc
   // per-lane byte offsets of the ldmatrix rows of this warp's two m16 tiles
   for (uint32_t it = 0;; ++it) {
     const int s = it % Gm::kStages;
-    if (!mbar_wait(full0 + 8 * s, (it / Gm::kStages) & 1, a.error_flag)) return;
+    // waits are voted warp-wide, so a timed-out warp leaves as a whole (the
+    // epilogue's shuffles name every lane)
+    if (!__all_sync(0xffffffffu, mbar_wait(full0 + 8 * s, (it / Gm::kStages) & 1, a.error_flag))) return;
     const UnitMeta mu = meta[s];
     if (mu.end) break;
     if (mu.wgen != cur_gen) {
       __syncwarp();
       if (cur_gen >= 0 && lane == 0) mbar_arrive(wfree);  // done with the previous fragments
-      if (!mbar_wait(wfull, mu.wgen & 1, a.error_flag)) return;
+      if (!__all_sync(0xffffffffu, mbar_wait(wfull, mu.wgen & 1, a.error_flag))) return;
       cur_gen = mu.wgen;
     }
     const uint32_t stage = stage0 + s * Gm::kStageBytes;

@@ -57,6 +57,8 @@ _SIGNATURES = {
     "kvc_calibration_workspace_doubles": (c_int64, [c_int64, c_int, c_int, c_int]),
     "kvc_calibration_accumulate": (
         c_int, [_P, c_int, c_int64, c_int64, c_int, c_int, c_int, _P, _P, _P, _P, _P, c_int64, _P]),
+    "kvc_calibration_accumulate_post_rope": (
+        c_int, [_P, c_int, c_int64, c_int64, c_int, c_int, c_int, c_int64, _P, _P, _P, _P, _P, _P, c_int64, _P]),
     "kvc_shift_positions": (c_int, [_P, _P, c_int, _P, c_int64, c_int64, _P, _P, _P]),
     "kvc_calibration_accumulate_noalloc": (
         c_int, [_P, c_int, c_int64, c_int64, c_int, c_int, c_int, _P, _P, _P, _P, _P]),

@@ -62,7 +62,15 @@ class LayerAccumulator:
         self.count = 0
         self._ws: torch.Tensor | None = None
 
-    def add(self, projected: torch.Tensor, heads: int, head_dim: int, rotary_dim: int) -> None:
+    def add(self, projected: torch.Tensor, heads: int, head_dim: int, rotary_dim: int, *,
+            first_position: int | None = None, omega: torch.Tensor | None = None) -> None:
+        """Add one batch of query rows.
+
+        Pre-RoPE projections by default (the stats builder's input).  With
+        ``first_position`` and ``omega`` the rows are post-RoPE attention inputs
+        at positions ``first_position + t``; the reduction undoes the rotation
+        in fp32 before summing.
+        """
         expected = heads * head_dim
         if projected.shape[-1] == expected * 2:
             projected = projected[..., :expected]  # Qwen3.5 packs the output gate after Q
@@ -89,7 +97,7 @@ class LayerAccumulator:
         if self._ws is None or self._ws.numel() < need:
             self._ws = torch.empty(max(need, 1), dtype=torch.float64, device=dev)
         K.calibration_accumulate(rows, heads, head_dim, rotary_dim, self.real_sum, self.imag_sum, self.abs_sum,
-                                 self.pass_sum, self._ws)
+                                 self.pass_sum, self._ws, first_position=first_position, omega=omega)
         self.count += rows.shape[0]
 
     def means(self) -> dict[str, torch.Tensor]:

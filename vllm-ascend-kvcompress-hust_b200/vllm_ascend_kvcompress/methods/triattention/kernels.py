@@ -250,17 +250,32 @@ def calibration_workspace_doubles(n_tokens: int, heads: int, head_dim: int, rota
 
 
 def calibration_accumulate(q: torch.Tensor, heads: int, head_dim: int, rotary_dim: int, re_sum, im_sum,
-                           abs_sum, pass_sum, workspace) -> None:
-    """Add per-(head, frequency) sums of pre-RoPE queries ``q [tokens, >= heads*head_dim]``."""
-    require_cuda(q, re_sum, workspace)
+                           abs_sum, pass_sum, workspace, *, first_position: int | None = None,
+                           omega: torch.Tensor | None = None) -> None:
+    """Add per-(head, frequency) sums of queries ``q [tokens, >= heads*head_dim]``.
+
+    Pre-RoPE rows by default; with ``first_position`` and ``omega`` the rows are
+    post-RoPE at positions ``first_position + t`` and the rotation is undone in
+    fp32 inside the reduction (no intermediate 16-bit rounding).
+    """
+    require_cuda(q, re_sum, workspace, omega)
     if q.ndim != 2 or q.stride(1) != 1:
         raise RuntimeError("calibration queries must be [tokens, width] with a contiguous last dim")
     for t, n in ((re_sum, "re_sum"), (im_sum, "im_sum"), (abs_sum, "abs_sum"), (workspace, "workspace")):
         _need(t, torch.float64, n)
-    N.check(N.lib().kvc_calibration_accumulate(
-        _p(q), _dtype_code(q.dtype), q.shape[0], q.stride(0), heads, head_dim, rotary_dim, _p(re_sum),
-        _p(im_sum), _p(abs_sum), _p(pass_sum), _p(workspace), workspace.numel(), _stream()),
-        "kvc_calibration_accumulate")
+    if (first_position is None) != (omega is None):
+        raise ValueError("first_position and omega go together (post-RoPE rows)")
+    if omega is None:
+        N.check(N.lib().kvc_calibration_accumulate(
+            _p(q), _dtype_code(q.dtype), q.shape[0], q.stride(0), heads, head_dim, rotary_dim, _p(re_sum),
+            _p(im_sum), _p(abs_sum), _p(pass_sum), _p(workspace), workspace.numel(), _stream()),
+            "kvc_calibration_accumulate")
+        return
+    _need(omega, torch.float32, "omega")
+    N.check(N.lib().kvc_calibration_accumulate_post_rope(
+        _p(q), _dtype_code(q.dtype), q.shape[0], q.stride(0), heads, head_dim, rotary_dim, int(first_position),
+        _p(omega), _p(re_sum), _p(im_sum), _p(abs_sum), _p(pass_sum), _p(workspace), workspace.numel(), _stream()),
+        "kvc_calibration_accumulate_post_rope")
 
 
 def unrotate_queries(q: torch.Tensor, heads: int, head_dim: int, rotary_dim: int, first_position: int,

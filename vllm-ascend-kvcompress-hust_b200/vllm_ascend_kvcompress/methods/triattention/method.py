@@ -249,7 +249,7 @@ class TriAttentionMethod(KVCompressionMethod):
                 fill[slot] = W
 
     def complete_query_observation(self, observation: QueryObservation) -> None:
-        """Undo RoPE of the buffered rows (positions end at ``semantic_num_tokens``) and reduce them.
+        """Reduce the buffered rows with their RoPE undone (positions end at ``semantic_num_tokens``).
 
         Once a layer has accumulated ``online_calibration_min_tokens`` rows, its
         q_mean_real / q_mean_imag / q_abs_mean (and q_pass_mean) are replaced in
@@ -263,11 +263,10 @@ class TriAttentionMethod(KVCompressionMethod):
         for slot, n in enumerate(fill):
             if n <= 0:
                 continue
-            rows = buf[slot, :n]
-            K.unrotate_queries(rows, heads, self.head_dim, self.rotary_dim,
-                               int(observation.semantic_num_tokens) - n, self.scoring_omega[slot])
+            # the reduction un-rotates in fp32 registers: no rounding back to 16 bits
             acc = self._online_sums[slot]
-            acc.add(rows, heads, self.head_dim, self.rotary_dim)
+            acc.add(buf[slot, :n], heads, self.head_dim, self.rotary_dim,
+                    first_position=int(observation.semantic_num_tokens) - n, omega=self.scoring_omega[slot])
             if acc.count >= self.config.online_calibration_min_tokens:
                 self._publish_online_stats(slot, acc)
         self._free_buffers.append(buf)
