@@ -62,7 +62,7 @@ def test_noalloc_matches_workspace_entry_on_two_calls(heads, head_dim, rot, size
 def test_noalloc_refuses_geometry_beyond_its_scratch():
     lib = N.lib()
     # one partial row holds 3 * heads * (rot/2 + head_dim - rot) doubles
-    heads, head_dim, rot = 4096, 128, 128
+    heads, head_dim, rot = 8192, 128, 128
     assert 3 * heads * (rot // 2) > N.CALIB_STATIC_SCRATCH_DOUBLES
     sums = _sums(heads, rot // 2, 0)
     q = torch.zeros(1, 8, dtype=torch.bfloat16, device="cuda")  # never read: refused up front
