@@ -45,6 +45,7 @@ extern "C" {
 #define KVC_DEV_TOKEN_RANGE 2   /* a keep index outside [0, tokens) */
 #define KVC_DEV_BUDGET 4        /* budget/windows impossible for a request */
 #define KVC_DEV_TIMEOUT 8       /* a bounded pipeline wait expired (the kernel gave up) */
+#define KVC_DEV_INDEX_RANGE 16  /* a request index outside the offsets table */
 
 /* cache element types */
 #define KVC_BF16 0
@@ -298,11 +299,55 @@ int kvc_unrotate_queries(void* q, int dtype, int64_t n_tokens, int64_t row_strid
 /*
  * Physical decode positions: out[i] = positions[i] - offsets[request_indices[i]].
  * Replaces shift_positions (methods/triattention/kernels.py:35-47).
- * index_bytes: 4 (int32 request indices) or 8 (int64).
+ * index_bytes: 4 (int32 request indices) or 8 (int64).  An index outside
+ * [0, num_offsets) raises KVC_DEV_INDEX_RANGE and passes the position through.
  */
 int kvc_shift_positions(const int64_t* positions, const void* request_indices, int index_bytes,
                         const int64_t* offsets, int64_t num_offsets, int64_t n, int64_t* out,
                         int32_t* error_flag, void* stream);
+
+/*
+ * Decode-step offsets of compressed requests in one launch:
+ *   physical_positions[i] = positions[i] - offsets[request_indices[i]]   (i < num_tokens)
+ *   semantic_seq_lens[r] = seq_lens[r]; seq_lens[r] -= offsets[r]        (r < num_reqs)
+ * Either part may be empty (num_tokens = 0, or num_reqs = 0 with seq_lens NULL),
+ * so a host can shift the slot-mapping positions and, later in the step, the
+ * attention lengths.  semantic_seq_lens may be NULL (no copy kept).  Requests
+ * never compressed carry offset 0.  Replaces the device work of
+ * AscendKVCompressionProvider.physical_positions_for_slot_mapping
+ * (provider.py:687-705, i.e. shift_positions, methods/triattention/kernels.py:35-47)
+ * and of apply_physical_attention_lengths (provider.py:707-728: the semantic
+ * copy and seq_lens.sub_(offsets)); the host-side optimistic lengths stay host work.
+ * index_bytes: 4 or 8 (request_indices); len_bytes: 4 or 8 (seq_lens and
+ * semantic_seq_lens).  A request index, or a row r, outside [0, num_offsets)
+ * raises KVC_DEV_INDEX_RANGE and leaves that value unshifted.
+ */
+int kvc_decode_offsets(const int64_t* positions, const void* request_indices, int index_bytes,
+                       int64_t num_tokens, const int64_t* offsets, int64_t num_offsets,
+                       int64_t* physical_positions, void* seq_lens, void* semantic_seq_lens, int len_bytes,
+                       int num_reqs, int32_t* error_flag, void* stream);
+
+/*
+ * Scheduler pages -> kernel blocks: out[i] = ids[i / blocks_per_page] *
+ * blocks_per_page + i % blocks_per_page for i < n_ids * blocks_per_page.
+ * Replaces _expand_scheduler_block_ids (provider.py:1273-1287), which turns a
+ * 1152- or 2048-token logical page into 9 or 16 consecutive 128-token blocks.
+ * (The step below expands inside its block-table gather when
+ * kvc_triattention_step.cache_blocks_per_page > 1.)
+ */
+int kvc_expand_block_ids(const int64_t* ids, int64_t n_ids, int blocks_per_page, int64_t* out, void* stream);
+
+/*
+ * Commit staging alone: staged_rows[r][i] = the scheduler page id of request
+ * r's i-th destination page (its first kernel block / blocks_per_page; -1 past
+ * the request's pages, i < staged_row_stride) and staged_offsets[r] =
+ * semantic[r] - budget.  With blocks_per_page = 1 this is the staging that
+ * kvc_compact performs.  Replaces the inputs of PendingCompression and of the
+ * offset rows (provider.py:38-54, 981-1010).
+ */
+int kvc_stage_commit(const int64_t* dst_blocks, const int64_t* dst_block_off, int num_requests,
+                     int blocks_per_page, int64_t* staged_rows, int staged_row_stride,
+                     int64_t* staged_offsets, const int64_t* semantic, int budget, void* stream);
 
 /*
  * Tensor-parallel score sync over NVLink peer memory, replacing the MAX
@@ -375,7 +420,9 @@ int kvc_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
  * seven.  Stages:
  *   KVC_STAGE_TABLES    gather the per-request block tables (src_tables /
  *                       dst_tables: device arrays of device pointers) into
- *                       the CSR arrays src_blocks / dst_blocks
+ *                       the CSR arrays src_blocks / dst_blocks, expanding
+ *                       scheduler pages into kernel blocks on the way
+ *                       (cache_blocks_per_page)
  *   KVC_STAGE_SCORE     prepare fragments/coefficients, score, head stats and
  *                       normalise into rows (kvc_prepare_score_fragments +
  *                       kvc_score_paged_keys_tc, or the FMA pair; kvc_head_stats;
@@ -461,6 +508,11 @@ typedef struct kvc_triattention_step {
   int32_t staged_row_stride;
   int64_t* staged_offsets;
   int32_t* error_flag;
+  /* kernel blocks per entry of src_tables / dst_tables (scheduler pages of
+   * 128 * cache_blocks_per_page tokens); 0 or 1: the entries are kernel
+   * blocks.  Under KVC_STAGE_COMPACT with staging, staged rows then hold
+   * scheduler page ids. */
+  int32_t cache_blocks_per_page;
 } kvc_triattention_step;
 
 int64_t kvc_triattention_step_size(void);   /* sizeof(kvc_triattention_step), for bindings */

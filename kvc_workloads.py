@@ -81,8 +81,10 @@ class Workload:
     seed: int
     cache_blocks_per_page: int = 1     # scheduler page / 128-token kernel block
     pool_pages: int | None = None      # kernel blocks in the shuffled source pool
-    src_tables: list[list[int]] = field(default_factory=list)
+    src_tables: list[list[int]] = field(default_factory=list)   # kernel block ids (expanded)
     dst_tables: list[list[int]] = field(default_factory=list)
+    src_pages: list[list[int]] = field(default_factory=list)    # scheduler page ids (unexpanded)
+    dst_pages: list[list[int]] = field(default_factory=list)
     num_blocks: int = 0
 
     @property
@@ -116,22 +118,26 @@ def place_blocks(w: Workload) -> Workload:
         raise ValueError("pool too small for the sequences")
     g = torch.Generator().manual_seed(w.seed + SALT_TABLE)
     perm = torch.randperm(pool_pages, generator=g).tolist()
-    src, pos = [], 0
+    src, src_pages, pos = [], [], 0
     for n in need:
         pages = perm[pos:pos + n]
         pos += n
+        src_pages.append(pages)
         src.append([p * per + j for p in pages for j in range(per)])
     dst_pages_per_req = _pages(w.options.kv_budget, per)
     nxt = pool_pages
-    dst = []
+    dst, dst_pages = [], []
     for i in range(len(w.lengths)):
         if i in w.compressed():
             pages = list(range(nxt, nxt + dst_pages_per_req))
             nxt += dst_pages_per_req
+            dst_pages.append(pages)
             dst.append([p * per + j for p in pages for j in range(per)])
         else:
+            dst_pages.append([])
             dst.append([])
     w.src_tables, w.dst_tables, w.num_blocks = src, dst, nxt * per
+    w.src_pages, w.dst_pages = src_pages, dst_pages
     return w
 
 
@@ -313,17 +319,23 @@ def b200_method(w: Workload, caches, stats_path: str, *, tp_size: int = 1, tp_gr
     return m
 
 
-def b200_requests(w: Workload, device="cuda", indices: list[int] | None = None):
-    """CompressionRequest objects of the workload's compressed sequences."""
+def b200_requests(w: Workload, device="cuda", indices: list[int] | None = None, pages: bool = False):
+    """CompressionRequest objects of the workload's compressed sequences.
+
+    ``pages``: the device tables hold scheduler page ids (for
+    ``compress_many(..., cache_blocks_per_page=w.cache_blocks_per_page)``)
+    instead of kernel block ids.
+    """
     from vllm_ascend_kvcompress.methods.base import CompressionRequest
 
+    src_t, dst_t = (w.src_pages, w.dst_pages) if pages else (w.src_tables, w.dst_tables)
     out = []
     for i in (indices if indices is not None else w.compressed()):
         out.append(CompressionRequest(
             request_id=f"r{i}", semantic_num_tokens=w.lengths[i], physical_num_tokens=w.lengths[i],
-            source_block_ids=(tuple(w.src_tables[i]),), destination_block_ids=(tuple(w.dst_tables[i]),),
-            source_block_ids_device=torch.tensor(w.src_tables[i], dtype=torch.long, device=device),
-            destination_block_ids_device=torch.tensor(w.dst_tables[i], dtype=torch.long, device=device)))
+            source_block_ids=(tuple(w.src_pages[i]),), destination_block_ids=(tuple(w.dst_pages[i]),),
+            source_block_ids_device=torch.tensor(src_t[i], dtype=torch.long, device=device),
+            destination_block_ids_device=torch.tensor(dst_t[i], dtype=torch.long, device=device)))
     return out
 
 

@@ -174,7 +174,7 @@ def test_header_compiles_as_c_and_links(tmp_path):
         "#include <stddef.h>\n#include <stdio.h>\n#include \"kvc.h\"\n"
         "int main(void) {\n"
         "  printf(\"%d %lld %zu\\n\", kvc_abi_version(), (long long)kvc_triattention_step_size(),\n"
-        "         offsetof(kvc_triattention_step, error_flag));\n"
+        "         offsetof(kvc_triattention_step, cache_blocks_per_page));\n"
         "  return 0;\n}\n")
     libdir = N.library_path().parent
     exe = tmp_path / "t"
@@ -185,4 +185,4 @@ def test_header_compiles_as_c_and_links(tmp_path):
     out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()
     assert int(out[0]) == N.ABI_VERSION
     assert int(out[1]) == ctypes.sizeof(N.TriAttentionStep)
-    assert int(out[2]) == N.TriAttentionStep.error_flag.offset
+    assert int(out[2]) == N.TriAttentionStep.cache_blocks_per_page.offset

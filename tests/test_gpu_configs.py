@@ -1,0 +1,104 @@
+"""GPU parity at the benchmark configurations' own shapes (CUDA path vs the CPU oracle).
+
+The golden-vector and edge-case suites use small geometries; these cases run
+the specification's shapes, reduced in batch size (and with layer caches
+aliased round-robin, which repeats the same per-layer work) only where host
+memory and the oracle's run time require it:
+
+* config 1: 48 layers, 40 query / 8 KV heads, head_dim 128, theta 1e6,
+  kv_budget 4608, V3 with prefix 128 / recent 512 / 8 segments, at
+  score_layer_stride 8 (default) and 1, sequences spanning 4,736-32,768 tokens;
+* config 2: the Qwen3.5 full-attention layout -- 16 query / 2 KV heads,
+  head_dim 256 with partial RoPE over 64 dims, theta 1e7, 10 layers at stride 2,
+  2048-token scheduler pages of 16 kernel blocks handed over unexpanded,
+  kv_budget 4608, sequences up to 52k tokens;
+* config 3: one full calibration layer, 64 x 8192 tokens x 40 heads x 128,
+  against an fp64 reduction of the same tensor at |d| <= 1e-4 * max(|ref|, mean|q|).
+
+Bars: scores within 1e-3 * max(|ref|, 1); keep indices identical except at
+near ties; compacted K/V bytes identical.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import kvc_workloads as W
+from gpu_cases import assert_compaction, assert_scores_close, assert_selection, bind, oracle_select, page_offsets
+
+pytestmark = pytest.mark.gpu
+
+
+def _config1(stride: int, lengths: list[int]) -> W.Workload:
+    geo = W.Geometry(48, 8, 40, 128, 128, 1e6)
+    opts = W.Options(kv_budget=4608, recompute_window=128, protected_prefix_window=128,
+                     protected_recent_window=512, score_layer_stride=stride)
+    return W.place_blocks(W.Workload("config1", geo, opts, lengths, seed=31))
+
+
+def _config2() -> W.Workload:
+    geo = W.Geometry(10, 2, 16, 256, 64, 1e7, model_type="qwen3_5_moe_text")
+    opts = W.Options(kv_budget=4608, recompute_window=1024, protected_prefix_window=128,
+                     protected_recent_window=512, score_layer_stride=2)
+    return W.place_blocks(W.Workload("config2", geo, opts, [8192, 30000, 52000], seed=22,
+                                     cache_blocks_per_page=16))
+
+
+def _run(w: W.Workload, distinct: int, tmp_path, bpp: int = 1) -> None:
+    n = w.geometry.num_layers
+    cpu = [W.kv_pages(w, layer) for layer in range(distinct)]
+    gpu = [(k.cuda(), v.cuda()) for k, v in cpu]
+    cpu_all = [cpu[layer % distinct] for layer in range(n)]
+    gpu_all = [gpu[layer % distinct] for layer in range(n)]
+    m = bind(w, gpu_all, tmp_path)
+    assert m.use_tensor_scorer
+    reqs = W.b200_requests(w, pages=bpp > 1)
+    keep = m.select_many(reqs, cache_blocks_per_page=bpp).cpu()
+    agg = m.last_stats[3].detach().cpu()
+    idx = w.compressed()
+    ref = oracle_select(w, cpu_all, idx)
+    offs = page_offsets(w, idx)
+    for row, i in enumerate(idx):
+        ref_agg, ref_keep = ref[i]
+        assert_scores_close(agg[offs[row]: offs[row] + w.lengths[i]], ref_agg)
+        assert_selection(w, ref_agg, ref_keep, keep[row])
+    m.compress_many(reqs, stage_commit=True, cache_blocks_per_page=bpp)
+    m.check_device_errors()
+    torch.cuda.synchronize()
+    assert_compaction(w, cpu, gpu, {i: keep[row] for row, i in enumerate(idx)})
+    assert m.staged_offsets.cpu().tolist() == [w.lengths[i] - w.options.kv_budget for i in idx]
+
+
+def test_config1_shape_default_stride(tmp_path):
+    _run(_config1(8, [4736, 11000, 20000, 32768]), distinct=4, tmp_path=tmp_path)
+
+
+def test_config1_shape_every_layer_scored(tmp_path):
+    _run(_config1(1, [4736, 32768]), distinct=3, tmp_path=tmp_path)
+
+
+def test_config2_shape_with_scheduler_pages(tmp_path):
+    _run(_config2(), distinct=5, tmp_path=tmp_path, bpp=16)
+
+
+def test_config3_full_layer_against_fp64():
+    from vllm_ascend_kvcompress.methods.triattention import kernels as K
+
+    heads, hd, rot = 40, 128, 128
+    n_tok = 64 * 8192
+    q = W.calibration_queries(0, 64, 8192, heads, hd, device="cuda")
+    ws = torch.empty(K.calibration_workspace_doubles(n_tok, heads, hd, rot), dtype=torch.float64, device="cuda")
+    z = lambda: torch.zeros(heads, rot // 2, dtype=torch.float64, device="cuda")
+    re, im, ab = z(), z(), z()
+    K.calibration_accumulate(q, heads, hd, rot, re, im, ab, None, ws)
+    torch.cuda.synchronize()
+    v = q.view(-1, heads, hd).double()
+    f = rot // 2
+    ref = (v[..., :f].sum(0), v[..., f:rot].sum(0), torch.sqrt(v[..., :f].square() + v[..., f:rot].square()).sum(0))
+    mean_abs = float(v.abs().mean())
+    del v
+    for got, want in zip((re, im, ab), ref):
+        g_mean, w_mean = got / n_tok, want / n_tok
+        err = float((g_mean - w_mean).abs().max())
+        assert err <= 1e-4 * max(float(w_mean.abs().max()), mean_abs), err

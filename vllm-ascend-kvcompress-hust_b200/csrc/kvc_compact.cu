@@ -316,14 +316,17 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1) compact_bulk_kernel(const 
   bulk_wait_all();
 }
 
+// Commit staging of request r: its destination row (one entry per scheduler
+// page of `bpp` kernel blocks: the page id is its first block / bpp; entries
+// past the request's pages are -1) and its position offset semantic - budget.
 __global__ void stage_commit_kernel(const int64_t* __restrict__ dst_blocks, const int64_t* __restrict__ dst_block_off,
-                                    int R, int64_t* staged_rows, int stride, int64_t* staged_offsets,
+                                    int R, int bpp, int64_t* staged_rows, int stride, int64_t* staged_offsets,
                                     const int64_t* __restrict__ semantic, int budget) {
   const int r = blockIdx.x;
   const int64_t b0 = dst_block_off[r], b1 = dst_block_off[r + 1];
   if (staged_rows)
     for (int64_t i = threadIdx.x; i < stride; i += blockDim.x)
-      staged_rows[(int64_t)r * stride + i] = (b0 + i < b1) ? dst_blocks[b0 + i] : -1;
+      staged_rows[(int64_t)r * stride + i] = (b0 + i * bpp < b1) ? dst_blocks[b0 + i * bpp] / bpp : -1;
   if (staged_offsets && semantic && threadIdx.x == 0) staged_offsets[r] = semantic[r] - budget;
 }
 
@@ -367,7 +370,7 @@ __global__ void shift_positions_kernel(const int64_t* __restrict__ pos, const I*
   if (i >= n) return;
   const int64_t r = (int64_t)req[i];
   if (r < 0 || r >= num_offsets) {
-    raise_flag(flag, KVC_DEV_BLOCK_RANGE);
+    raise_flag(flag, KVC_DEV_INDEX_RANGE);
     out[i] = pos[i];
     return;
   }
@@ -500,11 +503,26 @@ extern "C" int kvc_compact(const void* const* k_layers, const void* const* v_lay
     if (rc != KVC_OK) return rc;
   }
   if (staged_rows || (staged_offsets && semantic)) {
-    stage_commit_kernel<<<R, 128, 0, st>>>(dst_blocks, dst_block_off, R, staged_rows, staged_row_stride,
+    stage_commit_kernel<<<R, 128, 0, st>>>(dst_blocks, dst_block_off, R, 1, staged_rows, staged_row_stride,
                                            staged_offsets, semantic, budget);
     return launch_status();
   }
   return KVC_OK;
+}
+
+extern "C" int kvc_stage_commit(const int64_t* dst_blocks, const int64_t* dst_block_off, int num_requests,
+                                int blocks_per_page, int64_t* staged_rows, int staged_row_stride,
+                                int64_t* staged_offsets, const int64_t* semantic, int budget, void* stream) {
+  KVC_CHECK_ARG(dst_blocks && dst_block_off, KVC_ENULL);
+  KVC_CHECK_ARG(staged_offsets == nullptr || semantic != nullptr, KVC_ENULL);
+  KVC_CHECK_ARG(num_requests >= 0 && blocks_per_page >= 1 && budget > 0, KVC_EINVAL);
+  KVC_CHECK_ARG(staged_rows == nullptr || staged_row_stride > 0, KVC_EINVAL);
+  if (num_requests == 0 || (!staged_rows && !staged_offsets)) return KVC_OK;
+  stage_commit_kernel<<<num_requests, 128, 0, (cudaStream_t)stream>>>(dst_blocks, dst_block_off, num_requests,
+                                                                      blocks_per_page, staged_rows,
+                                                                      staged_row_stride, staged_offsets, semantic,
+                                                                      budget);
+  return launch_status();
 }
 
 template <bool GATHER>

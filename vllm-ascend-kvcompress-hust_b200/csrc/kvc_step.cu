@@ -3,32 +3,48 @@
 // The stages call the same validated entry points a caller would call one by
 // one, in the same order on the same stream; only the host round trips
 // between them go away (one call and one argument block instead of seven).
+#include <climits>
+
 #include "kvc_common.cuh"
 
 namespace {
 
 // Block tables of R requests into CSR order: blockIdx.x = request, blockIdx.y = 0
-// source / 1 destination.
+// source / 1 destination.  A table entry is a scheduler page of `bpp`
+// consecutive 128-token kernel blocks: kernel block i of the request is
+// table[i / bpp] * bpp + i % bpp (bpp = 1: the entries are kernel blocks).
 __global__ void gather_tables_kernel(const int64_t* const* __restrict__ src_tables,
                                      const int64_t* __restrict__ src_off, int64_t* src_out,
                                      const int64_t* const* __restrict__ dst_tables,
-                                     const int64_t* __restrict__ dst_off, int64_t* dst_out) {
+                                     const int64_t* __restrict__ dst_off, int64_t* dst_out, int bpp) {
   const int r = blockIdx.x;
   const int64_t* const* tables = blockIdx.y ? dst_tables : src_tables;
   const int64_t* off = blockIdx.y ? dst_off : src_off;
   int64_t* out = blockIdx.y ? dst_out : src_out;
   const int64_t b = off[r], n = off[r + 1] - b;
   const int64_t* t = tables[r];
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) out[b + i] = __ldg(t + i);
+  if (bpp == 1) {
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) out[b + i] = __ldg(t + i);
+  } else {
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) out[b + i] = __ldg(t + i / bpp) * bpp + i % bpp;
+  }
+}
+
+// Scheduler page ids -> kernel block ids (one thread per output block).
+__global__ void expand_ids_kernel(const int64_t* __restrict__ ids, int64_t n_out, int bpp, int64_t* out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n_out) out[i] = __ldg(ids + i / bpp) * bpp + i % bpp;
 }
 
 int tables_stage(const kvc_triattention_step& s, cudaStream_t st) {
   KVC_CHECK_ARG(s.src_tables && s.src_blocks && s.src_block_off, KVC_ENULL);
   const bool dst = s.dst_tables != nullptr;
   KVC_CHECK_ARG(!dst || (s.dst_blocks && s.dst_block_off), KVC_ENULL);
+  KVC_CHECK_ARG(s.cache_blocks_per_page >= 0, KVC_EINVAL);
   if (s.num_requests <= 0) return KVC_OK;
   gather_tables_kernel<<<dim3((unsigned)s.num_requests, dst ? 2 : 1), 128, 0, st>>>(
-      s.src_tables, s.src_block_off, s.src_blocks, s.dst_tables, s.dst_block_off, s.dst_blocks);
+      s.src_tables, s.src_block_off, s.src_blocks, s.dst_tables, s.dst_block_off, s.dst_blocks,
+      s.cache_blocks_per_page > 1 ? s.cache_blocks_per_page : 1);
   return kvc::launch_status();
 }
 
@@ -81,6 +97,17 @@ int score_stage(const kvc_triattention_step& s, void* const* ev, void* stream) {
 
 extern "C" int64_t kvc_triattention_step_size(void) { return (int64_t)sizeof(kvc_triattention_step); }
 
+extern "C" int kvc_expand_block_ids(const int64_t* ids, int64_t n_ids, int blocks_per_page, int64_t* out,
+                                    void* stream) {
+  KVC_CHECK_ARG(ids && out, KVC_ENULL);
+  KVC_CHECK_ARG(n_ids >= 0 && blocks_per_page >= 1 && n_ids <= INT64_MAX / blocks_per_page, KVC_EINVAL);
+  const int64_t n_out = n_ids * blocks_per_page;
+  if (n_out == 0) return KVC_OK;
+  expand_ids_kernel<<<(unsigned)((n_out + 255) / 256), 256, 0, (cudaStream_t)stream>>>(ids, n_out, blocks_per_page,
+                                                                                         out);
+  return kvc::launch_status();
+}
+
 extern "C" int kvc_triattention_run(const kvc_triattention_step* step, int stages, void* const* ev, void* stream) {
   KVC_CHECK_ARG(step, KVC_ENULL);
   KVC_CHECK_ARG(stages > 0 && (stages & ~KVC_STAGE_ALL) == 0, KVC_EINVAL);
@@ -109,11 +136,19 @@ extern "C" int kvc_triattention_run(const kvc_triattention_step* step, int stage
   }
   if (stages & KVC_STAGE_COMPACT) {
     mark(ev, 6, st);
+    // staged rows name scheduler pages: with multi-block pages they are staged
+    // after the copy, one entry per page
+    const bool pages = s.cache_blocks_per_page > 1;
     rc = kvc_compact(s.k_layers, s.v_layers, s.compact_layers, s.block_stride_bytes, s.num_blocks, s.row_bytes,
                      s.src_blocks, s.src_block_off, s.dst_blocks, s.dst_block_off, s.keep, s.tokens, s.num_requests,
-                     s.budget, s.staged_rows, s.staged_row_stride, s.staged_offsets, s.semantic, s.error_flag,
-                     stream);
+                     s.budget, pages ? nullptr : s.staged_rows, s.staged_row_stride,
+                     pages ? nullptr : s.staged_offsets, s.semantic, s.error_flag, stream);
     if (rc != KVC_OK) return rc;
+    if (pages && (s.staged_rows || s.staged_offsets)) {
+      rc = kvc_stage_commit(s.dst_blocks, s.dst_block_off, s.num_requests, s.cache_blocks_per_page, s.staged_rows,
+                            s.staged_row_stride, s.staged_offsets, s.semantic, s.budget, stream);
+      if (rc != KVC_OK) return rc;
+    }
   }
   mark(ev, 7, st);
   return KVC_OK;

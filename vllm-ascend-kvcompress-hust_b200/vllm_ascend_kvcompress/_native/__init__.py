@@ -19,7 +19,7 @@ KVC_OK = 0
 STATUS = {0: "ok", -22: "EINVAL", -14: "ENULL", -71: "EALIGN", -95: "EUNSUPPORTED", -5: "ECUDA",
           -28: "ECAPACITY"}
 CALIB_STATIC_SCRATCH_DOUBLES = 1 << 20
-DEV_BLOCK_RANGE, DEV_TOKEN_RANGE, DEV_BUDGET, DEV_TIMEOUT = 1, 2, 4, 8
+DEV_BLOCK_RANGE, DEV_TOKEN_RANGE, DEV_BUDGET, DEV_TIMEOUT, DEV_INDEX_RANGE = 1, 2, 4, 8, 16
 TENSOR_MAP_BYTES = 128
 IPC_HANDLE_BYTES = 64
 TP_MAX_WORLD = 64
@@ -60,6 +60,10 @@ _SIGNATURES = {
     "kvc_calibration_accumulate_post_rope": (
         c_int, [_P, c_int, c_int64, c_int64, c_int, c_int, c_int, c_int64, _P, _P, _P, _P, _P, _P, c_int64, _P]),
     "kvc_shift_positions": (c_int, [_P, _P, c_int, _P, c_int64, c_int64, _P, _P, _P]),
+    "kvc_decode_offsets": (
+        c_int, [_P, _P, c_int, c_int64, _P, c_int64, _P, _P, _P, c_int, c_int, _P, _P]),
+    "kvc_expand_block_ids": (c_int, [_P, c_int64, c_int, _P, _P]),
+    "kvc_stage_commit": (c_int, [_P, _P, c_int, c_int, _P, c_int, _P, _P, c_int, _P]),
     "kvc_calibration_accumulate_noalloc": (
         c_int, [_P, c_int, c_int64, c_int64, c_int, c_int, c_int, _P, _P, _P, _P, _P]),
     "kvc_tp_exchange_flag_words": (c_int, [c_int]),
@@ -100,7 +104,7 @@ class TriAttentionStep(ctypes.Structure):
         ("dst_block_off", _P), ("round_start", _P), ("semantic", _P), ("src_tables", _P), ("dst_tables", _P),
         ("score_coef", _P), ("raw", _P), ("partial", _P), ("mean", _P), ("var", _P), ("den", _P), ("rows", _P),
         ("agg", _P), ("keep", _P), ("staged_rows", _P), ("staged_row_stride", c_int32), ("staged_offsets", _P),
-        ("error_flag", _P),
+        ("error_flag", _P), ("cache_blocks_per_page", c_int32),
     ]
 
 _lib: ctypes.CDLL | None = None

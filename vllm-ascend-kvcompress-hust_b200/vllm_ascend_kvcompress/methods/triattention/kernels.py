@@ -24,6 +24,9 @@ compact                        materialize_token_slots per layer (method.py:272-
 gather_slots / scatter_slots   _gather_slots / _write_slots (cache.py:18-45)
 calibration_accumulate         _LayerAccumulator.add (calibration.py:95-131)
 shift_positions                shift_positions (kernels.py:35-47)
+decode_offsets                 provider.py:687-728 (slot-mapping positions and
+                               seq_lens of compressed requests per decode step)
+expand_block_ids               _expand_scheduler_block_ids (provider.py:1273-1287)
 =============================  =====================================================
 """
 
@@ -98,6 +101,7 @@ class BatchPlan:
     src_tables: torch.Tensor | None = None
     dst_tables: torch.Tensor | None = None
     keep_alive: list | None = None  # converted block tables referenced by src/dst_tables
+    blocks_per_page: int = 1  # kernel blocks per entry of the src/dst tables (scheduler pages)
 
     @property
     def tok_total(self) -> int:
@@ -305,3 +309,62 @@ def shift_positions(positions: torch.Tensor, request_indices: torch.Tensor, requ
         request_offsets.numel(), positions.numel(), _p(output), _p(error_flag), _stream()),
         "kvc_shift_positions")
     return output
+
+
+def decode_offsets(request_offsets: torch.Tensor, *, positions: torch.Tensor | None = None,
+                   request_indices: torch.Tensor | None = None, physical_positions: torch.Tensor | None = None,
+                   seq_lens: torch.Tensor | None = None, semantic_seq_lens: torch.Tensor | None = None,
+                   num_reqs: int = 0, error_flag: torch.Tensor | None = None) -> None:
+    """One launch of the per-step decode offsets (provider.py:687-728).
+
+    ``physical_positions[i] = positions[i] - request_offsets[request_indices[i]]``
+    when ``positions`` is given, and for ``r < num_reqs``
+    ``semantic_seq_lens[r] = seq_lens[r]; seq_lens[r] -= request_offsets[r]`` when
+    ``seq_lens`` is given (in place; int32 or int64).
+    """
+    require_cuda(request_offsets, positions, request_indices, physical_positions, seq_lens, semantic_seq_lens)
+    _need(request_offsets, torch.int64, "request_offsets")
+    n = 0
+    if positions is not None:
+        if request_indices is None or physical_positions is None:
+            raise ValueError("positions need request_indices and physical_positions")
+        for t, name in ((positions, "positions"), (physical_positions, "physical_positions")):
+            _need(t, torch.int64, name)
+        if request_indices.dtype not in (torch.int32, torch.int64) or not request_indices.is_contiguous():
+            raise RuntimeError("request_indices must be a contiguous int32/int64 tensor")
+        n = positions.numel()
+        if request_indices.numel() < n or physical_positions.numel() < n:
+            raise ValueError("request_indices and physical_positions must cover every position")
+    len_bytes = 8
+    if seq_lens is not None:
+        if seq_lens.dtype not in (torch.int32, torch.int64) or not seq_lens.is_contiguous():
+            raise RuntimeError("seq_lens must be a contiguous int32/int64 tensor")
+        if semantic_seq_lens is not None and (semantic_seq_lens.dtype != seq_lens.dtype
+                                              or not semantic_seq_lens.is_contiguous()):
+            raise RuntimeError("semantic_seq_lens must match seq_lens' dtype")
+        if num_reqs < 0 or num_reqs > seq_lens.numel() or (
+                semantic_seq_lens is not None and num_reqs > semantic_seq_lens.numel()):
+            raise ValueError("num_reqs exceeds the length buffers")
+        len_bytes = seq_lens.element_size()
+    else:
+        num_reqs = 0
+    N.check(N.lib().kvc_decode_offsets(
+        _p(positions), _p(request_indices), request_indices.element_size() if request_indices is not None else 8, n,
+        _p(request_offsets), request_offsets.numel(), _p(physical_positions), _p(seq_lens), _p(semantic_seq_lens),
+        len_bytes, int(num_reqs), _p(error_flag), _stream()), "kvc_decode_offsets")
+
+
+def expand_block_ids(ids: torch.Tensor, blocks_per_page: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Scheduler page ids -> consecutive 128-token kernel block ids (provider.py:1273-1287)."""
+    require_cuda(ids)
+    _need(ids, torch.int64, "ids")
+    if blocks_per_page == 1 and out is None:
+        return ids
+    n = ids.numel() * blocks_per_page
+    if out is None:
+        out = torch.empty(n, dtype=torch.int64, device=ids.device)
+    elif out.dtype != torch.int64 or not out.is_contiguous() or out.numel() < n:
+        raise RuntimeError("out must be a contiguous int64 tensor of ids.numel() * blocks_per_page")
+    N.check(N.lib().kvc_expand_block_ids(_p(ids), ids.numel(), int(blocks_per_page), _p(out), _stream()),
+            "kvc_expand_block_ids")
+    return out[:n]

@@ -373,16 +373,23 @@ class TriAttentionMethod(KVCompressionMethod):
 
     # ---- batched extension ----------------------------------------------------
 
-    def compress_many(self, requests: Sequence[CompressionRequest], *, stage_commit: bool = False
-                      ) -> tuple[CompressionResult, ...]:
-        """Score, select and compact a whole step's requests with one launch per stage."""
+    def compress_many(self, requests: Sequence[CompressionRequest], *, stage_commit: bool = False,
+                      cache_blocks_per_page: int = 1) -> tuple[CompressionResult, ...]:
+        """Score, select and compact a whole step's requests with one launch per stage.
+
+        ``cache_blocks_per_page > 1``: the requests' device block tables hold
+        scheduler page ids, each page being that many consecutive 128-token
+        kernel blocks (the provider's 1152/2048-token logical pages); the
+        pages are expanded on the device while the tables are gathered, and
+        with ``stage_commit`` the staged rows hold page ids.
+        """
         reqs = tuple(requests)
         if not reqs:
             return ()
         self._require_bound()
         self._raise_pending_device_error()
         plan = self._plan([(r.physical_num_tokens, r.semantic_num_tokens, r.source_block_ids_device,
-                            r.destination_block_ids_device) for r in reqs])
+                            r.destination_block_ids_device) for r in reqs], bpp=cache_blocks_per_page)
         self._run_step(plan, compact=True, stage_commit=stage_commit)
         self._arm_error_check()
         if self._strict:
@@ -391,12 +398,14 @@ class TriAttentionMethod(KVCompressionMethod):
         return tuple(CompressionResult(physical_num_tokens=self.config.kv_budget,
                                        per_layer_physical_num_tokens=lengths) for _ in reqs)
 
-    def select_many(self, requests: Sequence[CompressionRequest]) -> torch.Tensor:
+    def select_many(self, requests: Sequence[CompressionRequest], *, cache_blocks_per_page: int = 1
+                    ) -> torch.Tensor:
         """Keep indices ``[R, kv_budget]`` (int64, sorted per row) without compaction."""
         reqs = tuple(requests)
         self._require_bound()
         plan = self._plan([(r.physical_num_tokens, r.semantic_num_tokens, r.source_block_ids_device,
-                            r.destination_block_ids_device) for r in reqs], need_destination=False)
+                            r.destination_block_ids_device) for r in reqs], need_destination=False,
+                          bpp=cache_blocks_per_page)
         self._run_step(plan, compact=False)
         return self._keep_view(len(reqs)).view(len(reqs), self.config.kv_budget).clone()
 
@@ -541,16 +550,19 @@ class TriAttentionMethod(KVCompressionMethod):
         if self.offsets is None or not self.layer_caches or self._ws is None:
             raise RuntimeError("TriAttention method is not bound to KV cache")
 
-    def _plan(self, items, need_destination: bool = True) -> K.BatchPlan:
+    def _plan(self, items, need_destination: bool = True, bpp: int = 1) -> K.BatchPlan:
         """Validate a batch on the host and stage its metadata on the device.
 
         The per-request block tables are not copied here: their device
         addresses travel with the metadata and the step's first stage gathers
-        them into the CSR arrays ``src_blocks`` / ``dst_blocks``.
+        them into the CSR arrays ``src_blocks`` / ``dst_blocks`` (expanding
+        scheduler pages of ``bpp`` kernel blocks).
         """
         budget = self.config.kv_budget
         bs = self.cache_block_size
         dev = self.offsets.device
+        if isinstance(bpp, bool) or not isinstance(bpp, int) or bpp < 1:
+            raise ValueError("cache_blocks_per_page must be a positive integer")
         tokens, sem, src_ptrs, dst_ptrs, keep_alive = [], [], [], [], []
         page_off = [0]
         dst_need = -(-budget // bs)
@@ -559,7 +571,7 @@ class TriAttentionMethod(KVCompressionMethod):
             if budget <= 0 or budget > t:
                 raise ValueError("budget must be in [1, token_count]")
             n = -(-t // bs)
-            if src.numel() < n:
+            if src.numel() < -(-n // bpp):
                 raise RuntimeError("source block table is shorter than the physical token count")
             if src.dtype != torch.int64 or src.device != dev or not src.is_contiguous():
                 src = src.to(device=dev, dtype=torch.int64).contiguous()
@@ -569,7 +581,7 @@ class TriAttentionMethod(KVCompressionMethod):
             sem.append(s)
             src_ptrs.append(src.data_ptr())
             if need_destination:
-                if dst is None or dst.numel() < dst_need:
+                if dst is None or dst.numel() < -(-dst_need // bpp):
                     raise RuntimeError("destination block table is shorter than kv_budget")
                 if dst.dtype != torch.int64 or dst.device != dev or not dst.is_contiguous():
                     dst = dst.to(device=dev, dtype=torch.int64).contiguous()
@@ -587,7 +599,8 @@ class TriAttentionMethod(KVCompressionMethod):
             src_blocks=src_blocks, src_off=i64[: R + 1], dst_blocks=dst_blocks, dst_off=i64[R + 1: 2 * R + 2],
             round_start=i64[2 * R + 2: 3 * R + 2], semantic=i64[3 * R + 2: q], tokens_host=tuple(tokens),
             max_dst_blocks=dst_need, src_tables=i64[q: q + R],
-            dst_tables=i64[q + R: q + 2 * R] if need_destination else None, keep_alive=keep_alive)
+            dst_tables=i64[q + R: q + 2 * R] if need_destination else None, keep_alive=keep_alive,
+            blocks_per_page=bpp)
 
     def _mark(self, name: str) -> None:
         if self.profiler is not None:
@@ -662,6 +675,7 @@ class TriAttentionMethod(KVCompressionMethod):
         st.semantic = plan.semantic.data_ptr()
         st.src_tables = plan.src_tables.data_ptr()
         st.dst_tables = K._p(plan.dst_tables)
+        st.cache_blocks_per_page = plan.blocks_per_page
         return st
 
     def _gather_tables(self, plan: K.BatchPlan) -> None:
@@ -693,11 +707,12 @@ class TriAttentionMethod(KVCompressionMethod):
         st.keep = ws.ptr("keep", R * self.config.kv_budget, i64)
         self._last_shape = (L, R, heads, tok)
         staged_rows = staged_off = None
+        row_len = -(-plan.max_dst_blocks // plan.blocks_per_page)  # staged entries are scheduler pages
         if compact and stage_commit:
-            staged_rows = ws.get("staged_rows", R * plan.max_dst_blocks, torch.int64).view(R, plan.max_dst_blocks)
+            staged_rows = ws.get("staged_rows", R * row_len, torch.int64).view(R, row_len)
             staged_off = ws.get("staged_off", R, torch.int64)
         st.staged_rows = K._p(staged_rows)
-        st.staged_row_stride = plan.max_dst_blocks
+        st.staged_row_stride = row_len
         st.staged_offsets = K._p(staged_off)
         tail = N.STAGE_AGGREGATE | N.STAGE_SELECT | (N.STAGE_COMPACT if compact else 0)
         tail_slots = (4, 5, 6, 7) if compact else (4, 5, 7)
@@ -779,6 +794,8 @@ class TriAttentionMethod(KVCompressionMethod):
             what.append("a request shorter than kv_budget or its protected windows")
         if bits & N.DEV_TIMEOUT:
             what.append("a pipeline wait that timed out")
+        if bits & N.DEV_INDEX_RANGE:
+            what.append("a request index outside the offsets table")
         return "TriAttention kernels rejected " + ", ".join(what)
 
 
