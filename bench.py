@@ -96,6 +96,24 @@ class StageTimer:
     def __init__(self) -> None:
         self.steps: list[list[tuple[str, torch.cuda.Event]]] = []
         self.active = False
+        self.stamps: list[torch.Tensor] = []  # per step: the exchange kernel's four %globaltimer stamps
+
+    def exchange_done(self, ex) -> None:
+        """Keep a device copy of the peer exchange's stamps of this step (read after the pass)."""
+        if self.active:
+            self.stamps.append(ex.stamps_view().clone())
+
+    def exchange_us(self) -> dict | None:
+        """Median rank-skew wait and exchange time inside the exchange kernel (this rank's clock)."""
+        if not self.stamps:
+            return None
+        t = torch.stack(self.stamps).cpu().double()
+        wait = (t[:, 1] - t[:, 0]) / 1e3
+        exch = (t[:, 3] - t[:, 1]) / 1e3
+        total = (t[:, 3] - t[:, 0]) / 1e3
+        med = lambda x: float(x.median())
+        return {"tp_wait_us": med(wait), "tp_exchange_us": med(exch), "tp_kernel_us": med(total),
+                "steps": int(t.shape[0])}
 
     def new_step(self) -> None:
         if self.active:
@@ -341,6 +359,7 @@ def parity_check(ctx, w: W.Workload, s: Sample) -> dict:
     from oracle import triattention_oracle as O
 
     g, o = w.geometry, w.options
+    torch.set_num_threads(os.cpu_count() or 1)  # torchrun defaults ranks to one thread
     stats, opts, offs = oracle_inputs(w)
     n = -(-s.tokens // W.BLOCK)
     dp = len(w.dst_tables[s.index])
@@ -573,6 +592,7 @@ def measure(ctx: Ctx, w: W.Workload, nd: int, steps: int, warmup: int, *, clocks
     m.profiler = None
     barrier(ctx)
     stages = timer.stage_ms()
+    tp_split = timer.exchange_us()
 
     # end to end through the public API with host buffers: the block tables come
     # from pinned host memory each step (one H2D copy into the provider's
@@ -627,7 +647,7 @@ def measure(ctx: Ctx, w: W.Workload, nd: int, steps: int, warmup: int, *, clocks
     d2h = out_rows.numel() * 8 + out_off.numel() * 8
 
     res = {"ms": ms, "e2e_ms": e2e_ms, "stages": stages, "clocks": clk, "h2d": h2d, "d2h": d2h, "kvh": kvh,
-           "tp_sync_mode": m.tp_sync_mode, "parity": None, "cpu_baseline": None}
+           "tp_sync_mode": m.tp_sync_mode, "parity": None, "cpu_baseline": None, "tp_split": tp_split}
     if check:
         s = collect_sample(ctx, w, m, physical, nd)
         if ctx.rank == 0:
@@ -676,6 +696,8 @@ def summarize(w: W.Workload, res: dict, world: int, nd: int) -> dict:
     if world > 1:
         out["tp_sync_us"] = st.get("tp_sync", 0.0) * 1e3
         out["tp_sync_path"] = res["tp_sync_mode"]
+        if res.get("tp_split"):
+            out["tp_sync_split"] = res["tp_split"]
     if res["cpu_baseline"]:
         out["cpu_baseline"] = {k: v for k, v in res["cpu_baseline"].items() if k != "seconds"}
     return out
@@ -811,8 +833,9 @@ def b200_arm(args) -> None:
         tf = ROOT / "profiles" / "traffic.json"
         if tf.is_file() and args.config == 1 and args.seqs == 32 and args.layers == 48 and world == 1:
             traffic = json.loads(tf.read_text()).get("compact_kernel_bytes_per_launch_config1")
-        # the peer exchange replaces the layer-reduction launch with two kernels
-        launches_per_step = 9 if res["tp_sync_mode"] == "peer" else 8
+        # tables, prepare, score, head stats, normalise, layer reduction (or the
+        # peer exchange kernel), select, compact
+        launches_per_step = 8
         line = {
             "metric": METRIC, "value": s["value"], "unit": UNIT, "value_is": "aggregate over all GPUs",
             "per_gpu": s["per_gpu"], "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -827,6 +850,7 @@ def b200_arm(args) -> None:
             "step_roofline": s["step_roofline"], "stages_ms": s["stages_ms"],
             "score_kernel": s.get("score_kernel"),
             "tp_sync_us": s.get("tp_sync_us"), "tp_sync_path": res["tp_sync_mode"] if world > 1 else "none",
+            "tp_sync_split": s.get("tp_sync_split"),
             "e2e": s["e2e"], "gpu_launches": launches_per_step * args.steps, "clocks": res["clocks"],
             "parity": s["parity"],
         }

@@ -370,13 +370,21 @@ int kvc_stage_commit(const int64_t* dst_blocks, const int64_t* dst_block_off, in
  * or max) and mapped NaN -> -inf, +inf -> 1e30; page padding is 0.  This is
  * bit-identical to kvc_aggregate_rows applied to the TP=1 rows.
  * epoch: a positive step counter, one larger on every call (flags are never
- * cleared).  Waits for other ranks are bounded (2 s); on expiry the kernels
- * raise KVC_DEV_TIMEOUT in error_flag and complete.
- * The rows and agg buffers must not be rewritten by the caller until the call
- * has completed on this rank's stream (the next step's normalisation is safe).
+ * cleared).  Waits for other ranks are bounded (2 s); on expiry the kernel
+ * raises KVC_DEV_TIMEOUT in error_flag and completes.  One kernel launch per
+ * call; when it completes on this rank's stream every rank has finished
+ * reading this rank's rows, so the next step's normalisation may rewrite them.
+ * num_layers <= 512.
+ * Flag words (kvc_tp_exchange_flag_words): ready[world], pushed[world], a CTA
+ * counter, the started epoch, then from word kvc_tp_exchange_stamp_word(world)
+ * (8-byte aligned when the flags are) four uint64 %globaltimer stamps of this
+ * rank's last step: first CTA start, first CTA to see every rank ready, last
+ * CTA done, every rank's scores pushed.  Stamp 1 - stamp 0 is the wait for the
+ * slowest rank; stamp 3 - stamp 1 the exchange itself.
  */
 #define KVC_TP_MAX_WORLD 64
 int kvc_tp_exchange_flag_words(int world);
+int kvc_tp_exchange_stamp_word(int world);
 int kvc_tp_exchange_max(const float* const* peer_rows, float* const* peer_agg, int32_t* const* peer_flags,
                         int world, int rank, int num_layers, int total_pages, const int32_t* tokens,
                         const int32_t* page_off, int num_requests, int layer_aggregation, int32_t epoch,

@@ -127,7 +127,8 @@ def test_step_rejects_bad_stage_masks_without_launch():
 def test_exchange_ipc_and_unrotate_validate_on_the_host():
     lib = N.lib()
     fake = ctypes.c_void_p(0x1000)
-    assert lib.kvc_tp_exchange_flag_words(8) == 17 and lib.kvc_tp_exchange_flag_words(0) == 0
+    assert lib.kvc_tp_exchange_flag_words(8) == 26 and lib.kvc_tp_exchange_flag_words(0) == 0
+    assert lib.kvc_tp_exchange_stamp_word(8) == 18 and lib.kvc_tp_exchange_stamp_word(8) % 2 == 0
     # exchange: NULL tables, rank outside the world, world above the maximum, epoch 0, bad aggregation
     assert lib.kvc_tp_exchange_max(None, fake, fake, 2, 0, 1, 1, fake, fake, 1, 0, 1, None, None) == -14
     assert lib.kvc_tp_exchange_max(fake, fake, fake, 2, 2, 1, 1, fake, fake, 1, 0, 1, None, None) == -22

@@ -2,8 +2,9 @@
 
 world = 1 runs the whole data path (signal, reduce, layer reduction, push,
 wait) against this rank's own buffers and must equal kvc_aggregate_rows bit
-for bit.  A world-2 call whose other rank never arrives must give up after
-its bounded wait, report KVC_DEV_TIMEOUT and leave the context usable.  The
+for bit, and leave its %globaltimer stamps in order.  A world-2 call whose
+other rank never arrives must give up after its bounded waits, report
+KVC_DEV_TIMEOUT and leave the context usable.  The
 two-GPU exchange is covered by test_gpu_tp_nccl.py.
 """
 
@@ -63,7 +64,10 @@ def test_single_rank_exchange_equals_aggregate_rows_bitwise(layer_agg):
         torch.cuda.synchronize()
         assert int(err.item()) == 0
         assert torch.equal(agg[0].view(torch.int32), ref.view(torch.int32))
-    assert flags[0].tolist() == [2, 2, 0]
+    assert flags[0].tolist()[:4] == [2, 2, 0, 2]  # ready, pushed, CTA counter, started epoch
+    w0 = lib.kvc_tp_exchange_stamp_word(1)
+    stamps = flags[0][w0: w0 + 8].view(torch.int64).tolist()
+    assert 0 < stamps[0] <= stamps[1] <= stamps[2] <= stamps[3]
 
 
 def test_exchange_rejects_bad_arguments_on_the_host():

@@ -67,6 +67,7 @@ _SIGNATURES = {
     "kvc_calibration_accumulate_noalloc": (
         c_int, [_P, c_int, c_int64, c_int64, c_int, c_int, c_int, _P, _P, _P, _P, _P]),
     "kvc_tp_exchange_flag_words": (c_int, [c_int]),
+    "kvc_tp_exchange_stamp_word": (c_int, [c_int]),
     "kvc_tp_exchange_max": (
         c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, _P, _P, c_int, c_int, c_int32, _P, _P]),
     "kvc_ipc_export": (c_int, [c_int, _P, _P, _P]),

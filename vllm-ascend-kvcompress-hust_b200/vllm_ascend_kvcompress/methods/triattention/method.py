@@ -728,6 +728,8 @@ class TriAttentionMethod(KVCompressionMethod):
             self._mark("tp_sync")
             ex.exchange(L, plan.total_pages, plan.tokens, plan.page_off, R, self.layer_aggregation_code, self._err,
                         K._stream())
+            if self.profiler is not None and hasattr(self.profiler, "exchange_done"):
+                self.profiler.exchange_done(ex)
             self._launch(tail & ~N.STAGE_AGGREGATE, tail_slots[1:])
         elif self.tensor_parallel_size > 1:
             self._launch(head, (0, 1, 2, 3))

@@ -136,6 +136,12 @@ class PeerScoreExchange:
     def agg_view(self, tok_total: int) -> torch.Tensor:
         return self.buf[self._agg_off: self._agg_off + 4 * tok_total].view(torch.float32)
 
+    def stamps_view(self) -> torch.Tensor:
+        """This rank's four %globaltimer stamps of the last exchange (int64 ns, device):
+        first CTA start, every rank ready, last CTA done, every rank's scores pushed."""
+        w = int(N.lib().kvc_tp_exchange_stamp_word(self.world))
+        return self.buf[4 * w: 4 * w + 32].view(torch.int64)
+
     def exchange(self, layers: int, total_pages: int, tokens: torch.Tensor, page_off: torch.Tensor,
                  num_requests: int, layer_aggregation: int, error_flag: torch.Tensor, stream: int) -> None:
         """Queue this rank's share of the step's sync on ``stream`` (all ranks call it each step)."""
