@@ -119,10 +119,13 @@ int kvc_score_paged_keys(const void* const* k_layers, int num_layers, int dtype,
  *   key_maps     host array of num_layers 128-byte TMA descriptors from
  *                kvc_encode_key_maps (built once per cache binding).
  *   frag         kvc_prepare_score_fragments output.
- *   partial_out  [L][total_pages*4][kvh*G][2]: (sum, sum of squared
- *                deviations from the partial's mean) per quarter page.
+ *   partial_out  [L][total_pages*parts][kvh*G][2]: (sum, sum of squared
+ *                deviations from the partial's mean) per 128/parts-token slice
+ *                of each page, parts = kvc_tc_partials_per_page() (the
+ *                consumer warps of a CTA, 4).
  */
 int kvc_tc_supported(int group, int head_dim, int rotary_dim);
+int kvc_tc_partials_per_page(void);
 int kvc_encode_key_maps(const void* const* k_layers, int num_layers, int dtype, int64_t block_stride,
                         int64_t num_blocks, int kv_heads, int head_dim, void* maps_out);
 int64_t kvc_fragment_words(int num_freq, int pass_dim);
@@ -142,7 +145,8 @@ int kvc_score_paged_keys_tc(const void* key_maps, int num_layers, int dtype, int
 /*
  * Per (scoring layer, request, query head) population mean/variance of the
  * raw scores, combined from the partial moments in fp64; denom = sqrt(max(var, 1e-6)).
- * parts_per_page: 1 (kvc_score_paged_keys) or 4 (kvc_score_paged_keys_tc).
+ * parts_per_page: 1 (kvc_score_paged_keys) or kvc_tc_partials_per_page()
+ * (kvc_score_paged_keys_tc); any divisor of 128.
  * Replaces torch.var_mean(raw, dim=-1, correction=0) (methods/triattention/method.py:379-381,423)
  * and the denominator of normalize_head_scores (methods/triattention/scoring.py:123-128).
  * mean_out, var_out, denom_out: [L][R][kvh*G].

@@ -308,7 +308,7 @@ def test_normalize_rows_equal_torch_fp32_bitwise(heads):
     assert torch.equal(rows[~nan].view(torch.int32), ref[~nan].view(torch.int32))
 
 
-@pytest.mark.parametrize("heads,parts", [(1, 4), (5, 4), (40, 4), (40, 1), (200, 4)])
+@pytest.mark.parametrize("heads,parts", [(1, 4), (5, 4), (40, 4), (40, 1), (200, 4), (40, 8), (5, 8)])
 def test_head_stats_match_fp64_var_mean(heads, parts):
     """kvc_head_stats from per-partial (sum, M2) equals torch.var_mean(correction=0) in fp64 within 1e-5."""
     lib = N.lib()

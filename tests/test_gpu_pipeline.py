@@ -138,7 +138,7 @@ def test_single_call_step_equals_entry_points_one_by_one(scorer, tmp_path, monke
                       r.destination_block_ids_device) for r in reqs])
     m2._gather_tables(plan)
     L, heads, R, tok = m2.scoring_layer_count, m2.local_kv_heads * m2.group, plan.num_requests, plan.tok_total
-    parts = 4 if m2.use_tensor_scorer else 1
+    parts = int(N.lib().kvc_tc_partials_per_page()) if m2.use_tensor_scorer else 1
     f32 = lambda n: torch.empty(n, dtype=torch.float32, device="cuda")
     raw, partial = f32(L * heads * tok), f32(L * plan.total_pages * parts * heads * 2)
     mean, var, den, rows, agg = f32(L * R * heads), f32(L * R * heads), f32(L * R * heads), f32(L * tok), f32(tok)

@@ -724,7 +724,7 @@ extern "C" int kvc_head_stats(const float* partial, int L, int R, int total_page
                               float* var_out, float* denom_out, void* stream) {
   KVC_CHECK_ARG(partial && tokens && page_off && mean_out && var_out && denom_out, KVC_ENULL);
   KVC_CHECK_ARG(L > 0 && R >= 0 && heads > 0 && total_pages >= 0, KVC_EINVAL);
-  KVC_CHECK_ARG(parts_per_page == 1 || parts_per_page == 4, KVC_EINVAL);
+  KVC_CHECK_ARG(parts_per_page > 0 && kBlock % parts_per_page == 0, KVC_EINVAL);
   if (R == 0) return KVC_OK;
   KVC_CHECK_ARG(heads <= 1024, KVC_EUNSUPPORTED);
   KVC_CHECK_ARG(R <= 65535, KVC_EINVAL);

@@ -543,6 +543,9 @@ extern "C" int kvc_tc_supported(int group, int head_dim, int rotary_dim) {
   return tc_geometry_supported(group, head_dim, rotary_dim) ? 1 : 0;
 }
 
+// One moments partial per consumer warp's 32-token slice of a page.
+extern "C" int kvc_tc_partials_per_page(void) { return kTcConsumers; }
+
 extern "C" int64_t kvc_fragment_words(int num_freq, int pass_dim) {
   if (num_freq <= 0 || num_freq % 16 || pass_dim < 0 || pass_dim % 16) return 0;
   return (int64_t)frag_steps(num_freq, pass_dim) * 32 * 4;

@@ -85,8 +85,8 @@ int score_stage(const kvc_triattention_step& s, void* const* ev, void* stream) {
   if (rc != KVC_OK) return rc;
   mark(ev, 2, st);
   rc = kvc_head_stats(s.partial, s.score_layers, s.num_requests, s.total_pages,
-                      s.scorer == KVC_SCORER_TENSOR ? 4 : 1, heads, s.tokens, s.page_off, s.mean, s.var, s.den,
-                      stream);
+                      s.scorer == KVC_SCORER_TENSOR ? kvc_tc_partials_per_page() : 1, heads, s.tokens, s.page_off,
+                      s.mean, s.var, s.den, stream);
   if (rc != KVC_OK) return rc;
   mark(ev, 3, st);
   return kvc_normalize_aggregate(s.raw, s.score_layers, heads, s.total_pages, s.mean, s.den, s.tokens, s.page_off,

@@ -39,6 +39,7 @@ _SIGNATURES = {
                 _P, c_int, c_int, _P, _P, _P, _P, _P]),
     "kvc_head_stats": (c_int, [_P, c_int, c_int, c_int, c_int, c_int, _P, _P, _P, _P, _P, _P]),
     "kvc_tc_supported": (c_int, [c_int, c_int, c_int]),
+    "kvc_tc_partials_per_page": (c_int, []),
     "kvc_encode_key_maps": (c_int, [_P, c_int, c_int, c_int64, c_int64, c_int, c_int, _P]),
     "kvc_fragment_words": (c_int64, [c_int, c_int]),
     "kvc_prepare_score_fragments": (

@@ -543,6 +543,7 @@ class TriAttentionMethod(KVCompressionMethod):
                                                self.local_kv_heads, self.head_dim)
             self.scoring_q_pass = stack(lambda c: c.stats.q_pass_mean) if self.pass_dim else None
             self.frag_block = K.fragment_words(self.num_freq, self.pass_dim)
+            self._tc_parts = int(N.lib().kvc_tc_partials_per_page())
 
     # ---- per-step pipeline ----------------------------------------------------
 
@@ -690,7 +691,7 @@ class TriAttentionMethod(KVCompressionMethod):
         L = self.scoring_layer_count
         heads = self.local_kv_heads * self.group
         R, tok = plan.num_requests, plan.tok_total
-        parts = 4 if self.use_tensor_scorer else 1
+        parts = self._tc_parts if self.use_tensor_scorer else 1
         st = self._set_plan(plan)
         f32, i64 = torch.float32, torch.int64
         if self.use_tensor_scorer:
