@@ -833,8 +833,8 @@ def b200_arm(args) -> None:
         tf = ROOT / "profiles" / "traffic.json"
         if tf.is_file() and args.config == 1 and args.seqs == 32 and args.layers == 48 and world == 1:
             traffic = json.loads(tf.read_text()).get("compact_kernel_bytes_per_launch_config1")
-        # tables, prepare, score, head stats, normalise, layer reduction (or the
-        # peer exchange kernel), select, compact
+        # tables, prepare, score, head stats, normalise, the layer reduction (or
+        # the peer exchange kernel), select, compact
         launches_per_step = 8
         line = {
             "metric": METRIC, "value": s["value"], "unit": UNIT, "value_is": "aggregate over all GPUs",

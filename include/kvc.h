@@ -442,8 +442,17 @@ int kvc_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
  *   KVC_STAGE_AGGREGATE layer reduction into agg (kvc_aggregate_rows)
  *   KVC_STAGE_SELECT    kvc_select_keep into keep
  *   KVC_STAGE_COMPACT   kvc_compact (+ commit staging when staged_rows/offsets)
- * A tensor-parallel caller runs TABLES | SCORE, all-reduces rows with MAX, then
- * runs AGGREGATE | SELECT | COMPACT.  stage_events (optional: KVC_STEP_EVENTS
+ *   KVC_STAGE_EXCHANGE  the tensor-parallel peer score sync: kvc_tp_exchange_max
+ *                       with peer_rows / peer_agg / peer_flags, world, rank
+ *                       and epoch (rows and agg must be this rank's buffers
+ *                       of the exchange); not together with AGGREGATE
+ * A tensor-parallel caller with the peer exchange runs TABLES | SCORE |
+ * EXCHANGE | SELECT | COMPACT in one call; with an NCCL all-reduce instead it
+ * runs TABLES | SCORE, all-reduces rows with MAX, then AGGREGATE | SELECT | COMPACT.
+ * When error_host is set, a call that runs SELECT or COMPACT ends by copying
+ * *error_flag to error_host (pinned host memory) and, when error_event is set,
+ * recording that cudaEvent_t after the copy, so the host can test the step's
+ * device errors later without a synchronisation.  stage_events (optional: KVC_STEP_EVENTS
  * cudaEvent_t handles, NULL entries skipped) are recorded on `stream` before
  * the prepare, score, head-stats, normalise, aggregate, select and compact
  * launches of the stages that run, and after the last launch, for per-stage
@@ -456,7 +465,8 @@ int kvc_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
 #define KVC_STAGE_SELECT 4
 #define KVC_STAGE_COMPACT 8
 #define KVC_STAGE_TABLES 16
-#define KVC_STAGE_ALL 31
+#define KVC_STAGE_ALL 31          /* the whole step with tensor parallelism off */
+#define KVC_STAGE_EXCHANGE 32     /* the peer score sync (kvc_tp_exchange_max); replaces AGGREGATE */
 #define KVC_STEP_EVENTS 8
 
 typedef struct kvc_triattention_step {
@@ -525,6 +535,16 @@ typedef struct kvc_triattention_step {
    * blocks.  Under KVC_STAGE_COMPACT with staging, staged rows then hold
    * scheduler page ids. */
   int32_t cache_blocks_per_page;
+  /* optional device-error read-back (see above) */
+  int32_t* error_host;
+  void* error_event;
+  /* KVC_STAGE_EXCHANGE: device arrays of `world` addresses (this rank's at `rank`) */
+  const float* const* peer_rows;
+  float* const* peer_agg;
+  int32_t* const* peer_flags;
+  int32_t world;
+  int32_t rank;
+  int32_t epoch;               /* one larger on every step */
 } kvc_triattention_step;
 
 int64_t kvc_triattention_step_size(void);   /* sizeof(kvc_triattention_step), for bindings */

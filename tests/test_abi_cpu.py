@@ -120,7 +120,9 @@ def test_step_rejects_bad_stage_masks_without_launch():
     st = N.TriAttentionStep()
     assert lib.kvc_triattention_run(None, N.STAGE_ALL, None, None) == -14
     assert lib.kvc_triattention_run(ctypes.byref(st), 0, None, None) == -22
-    assert lib.kvc_triattention_run(ctypes.byref(st), 32, None, None) == -22
+    assert lib.kvc_triattention_run(ctypes.byref(st), 64, None, None) == -22
+    assert lib.kvc_triattention_run(ctypes.byref(st), N.STAGE_EXCHANGE | N.STAGE_AGGREGATE, None, None) == -22
+    assert lib.kvc_triattention_run(ctypes.byref(st), N.STAGE_EXCHANGE, None, None) == -14  # no peer tables
     assert lib.kvc_triattention_run(ctypes.byref(st), N.STAGE_TABLES, None, None) == -14
 
 
@@ -175,7 +177,7 @@ def test_header_compiles_as_c_and_links(tmp_path):
         "#include <stddef.h>\n#include <stdio.h>\n#include \"kvc.h\"\n"
         "int main(void) {\n"
         "  printf(\"%d %lld %zu\\n\", kvc_abi_version(), (long long)kvc_triattention_step_size(),\n"
-        "         offsetof(kvc_triattention_step, cache_blocks_per_page));\n"
+        "         offsetof(kvc_triattention_step, epoch));\n"
         "  return 0;\n}\n")
     libdir = N.library_path().parent
     exe = tmp_path / "t"
@@ -186,4 +188,4 @@ def test_header_compiles_as_c_and_links(tmp_path):
     out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()
     assert int(out[0]) == N.ABI_VERSION
     assert int(out[1]) == ctypes.sizeof(N.TriAttentionStep)
-    assert int(out[2]) == N.TriAttentionStep.cache_blocks_per_page.offset
+    assert int(out[2]) == N.TriAttentionStep.epoch.offset

@@ -271,6 +271,62 @@ def test_calibration_partial_rope_unaligned_widths():
     torch.testing.assert_close(acc.pass_sum.float().cpu(), ref.pass_sum, rtol=1e-5, atol=1e-4)
 
 
+@pytest.mark.parametrize("heads,layer_agg", [(5, N.AGG_MEAN), (40, N.AGG_MEAN), (40, N.AGG_MAX), (1, N.AGG_MAX)])
+def test_normalize_aggregate_equals_torch_bitwise_with_near_ties(heads, layer_agg):
+    """Normalise + head max + layer reduction: rows and agg equal torch fp32 bit for bit, also where
+    several heads' quotients are within an ulp of each other."""
+    lib = N.lib()
+    lengths = [300, 2049, 128, 5000, 1]
+    pages = [-(-t // 128) for t in lengths]
+    off = [0]
+    for p in pages:
+        off.append(off[-1] + p)
+    P, L, R = off[-1], 4, len(lengths)
+    g = torch.Generator(device="cuda").manual_seed(40 + heads)
+    raw = torch.randn(L, P, heads, 128, generator=g, device="cuda") * 5 + 2
+    mean = torch.randn(L, R, heads, generator=g, device="cuda")
+    den = torch.rand(L, R, heads, generator=g, device="cuda") * 3 + 1e-3
+    req = torch.repeat_interleave(torch.arange(R, device="cuda"), torch.tensor(pages, device="cuda"))
+    if heads > 1:  # near ties: every head's quotient within a few ulps of head 0's on a band of tokens
+        mu, dn = mean[:, req, :, None], den[:, req, :, None]
+        q0 = (raw[:, :, :1] - mu[:, :, :1]) / dn[:, :, :1]
+        nudge = torch.randint(-3, 4, raw.shape, generator=g, device="cuda").float() * 2.0 ** -22
+        tied = q0 * (1 + nudge) * dn + mu
+        band = torch.zeros(128, dtype=torch.bool, device="cuda")
+        band[::3] = True
+        raw = torch.where(band, tied, raw)
+        raw[0, 0, :, 0] = raw[0, 0, 0, 0]  # exact duplicates
+    raw[0, 3, 0, 7] = float("nan")
+    raw[1, 2, heads - 1, 9] = float("inf")
+    raw[2, 5, 0, 0] = float("-inf")
+    tokens = torch.tensor(lengths, dtype=torch.int32, device="cuda")
+    page_off = torch.tensor(off, dtype=torch.int32, device="cuda")
+    mu, dn = mean[:, req, :, None], den[:, req, :, None]
+    ref_rows = ((raw - mu) / dn).amax(dim=2).reshape(L, P * 128)
+    pos = torch.arange(P * 128, device="cuda")
+    start = torch.repeat_interleave(torch.tensor(off[:-1], device="cuda"), torch.tensor(pages, device="cuda")) * 128
+    valid = (pos - start.repeat_interleave(128)) < tokens[req].long().repeat_interleave(128)
+    ref_rows = torch.where(valid[None], ref_rows, torch.zeros_like(ref_rows))
+    acc = ref_rows[0].clone()
+    for layer in range(1, L):
+        acc = acc + ref_rows[layer] if layer_agg == N.AGG_MEAN else torch.maximum(acc, ref_rows[layer])
+    if layer_agg == N.AGG_MEAN:
+        acc = acc / L
+    ref_agg = torch.where(valid, acc.nan_to_num(nan=float("-inf"), posinf=1e30, neginf=float("-inf")),
+                          torch.zeros_like(acc))
+    stream = torch.cuda.current_stream().cuda_stream
+    rows = torch.full((L, P * 128), 123.0, device="cuda")
+    agg = torch.full((P * 128,), 7.0, device="cuda")
+    assert lib.kvc_normalize_aggregate(raw.data_ptr(), L, heads, P, mean.data_ptr(), den.data_ptr(),
+                                       tokens.data_ptr(), page_off.data_ptr(), R, layer_agg, rows.data_ptr(),
+                                       agg.data_ptr(), stream) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(agg.view(torch.int32), ref_agg.view(torch.int32))
+    nan = torch.isnan(ref_rows)
+    assert torch.equal(torch.isnan(rows), nan)
+    assert torch.equal(rows[~nan].view(torch.int32), ref_rows[~nan].view(torch.int32))
+
+
 @pytest.mark.parametrize("heads", [1, 3, 5, 40])
 def test_normalize_rows_equal_torch_fp32_bitwise(heads):
     """kvc_normalize_aggregate rows == max over heads of (raw - mean) / den in IEEE fp32 (torch), padding 0."""

@@ -110,7 +110,8 @@ extern "C" int kvc_expand_block_ids(const int64_t* ids, int64_t n_ids, int block
 
 extern "C" int kvc_triattention_run(const kvc_triattention_step* step, int stages, void* const* ev, void* stream) {
   KVC_CHECK_ARG(step, KVC_ENULL);
-  KVC_CHECK_ARG(stages > 0 && (stages & ~KVC_STAGE_ALL) == 0, KVC_EINVAL);
+  KVC_CHECK_ARG(stages > 0 && (stages & ~(KVC_STAGE_ALL | KVC_STAGE_EXCHANGE)) == 0, KVC_EINVAL);
+  KVC_CHECK_ARG(!((stages & KVC_STAGE_EXCHANGE) && (stages & KVC_STAGE_AGGREGATE)), KVC_EINVAL);
   const kvc_triattention_step& s = *step;
   cudaStream_t st = (cudaStream_t)stream;
   int rc = KVC_OK;
@@ -126,6 +127,14 @@ extern "C" int kvc_triattention_run(const kvc_triattention_step* step, int stage
     mark(ev, 4, st);
     rc = kvc_aggregate_rows(s.rows, s.score_layers, s.total_pages, s.tokens, s.page_off, s.num_requests,
                             s.layer_aggregation, s.agg, stream);
+    if (rc != KVC_OK) return rc;
+  }
+  if (stages & KVC_STAGE_EXCHANGE) {
+    mark(ev, 4, st);
+    KVC_CHECK_ARG(s.peer_rows && s.peer_agg && s.peer_flags, KVC_ENULL);
+    rc = kvc_tp_exchange_max(s.peer_rows, s.peer_agg, s.peer_flags, s.world, s.rank, s.score_layers,
+                             s.total_pages, s.tokens, s.page_off, s.num_requests, s.layer_aggregation, s.epoch,
+                             s.error_flag, stream);
     if (rc != KVC_OK) return rc;
   }
   if (stages & KVC_STAGE_SELECT) {
@@ -151,5 +160,12 @@ extern "C" int kvc_triattention_run(const kvc_triattention_step* step, int stage
     }
   }
   mark(ev, 7, st);
+  if (s.error_host && s.error_flag && (stages & (KVC_STAGE_SELECT | KVC_STAGE_COMPACT))) {
+    if (cudaMemcpyAsync(s.error_host, s.error_flag, sizeof(int32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        (s.error_event && cudaEventRecord((cudaEvent_t)s.error_event, st) != cudaSuccess)) {
+      cudaGetLastError();
+      return KVC_ECUDA;
+    }
+  }
   return KVC_OK;
 }

@@ -84,6 +84,7 @@ _SIGNATURES = {
 
 SCORER_TENSOR, SCORER_FMA = 0, 1
 STAGE_SCORE, STAGE_AGGREGATE, STAGE_SELECT, STAGE_COMPACT, STAGE_TABLES, STAGE_ALL = 1, 2, 4, 8, 16, 31
+STAGE_EXCHANGE = 32
 STEP_EVENTS = 8
 STEP_EVENT_NAMES = ("prepare", "score", "head_stats", "normalize", "aggregate_rows", "select", "compact", "end")
 
@@ -107,6 +108,9 @@ class TriAttentionStep(ctypes.Structure):
         ("score_coef", _P), ("raw", _P), ("partial", _P), ("mean", _P), ("var", _P), ("den", _P), ("rows", _P),
         ("agg", _P), ("keep", _P), ("staged_rows", _P), ("staged_row_stride", c_int32), ("staged_offsets", _P),
         ("error_flag", _P), ("cache_blocks_per_page", c_int32),
+        ("error_host", _P), ("error_event", _P),
+        ("peer_rows", _P), ("peer_agg", _P), ("peer_flags", _P), ("world", c_int32), ("rank", c_int32),
+        ("epoch", c_int32),
     ]
 
 _lib: ctypes.CDLL | None = None

@@ -75,7 +75,11 @@ def _need(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
         raise RuntimeError(f"{name} must be a contiguous {dtype} tensor")
 
 
-@dataclass
+_PLAN_FIELDS = ("num_requests", "total_pages", "tokens", "page_off", "src_blocks", "src_off", "dst_blocks",
+                "dst_off", "round_start", "semantic", "tokens_host", "max_dst_blocks", "src_tables", "dst_tables",
+                "keep_alive", "blocks_per_page")
+
+
 class BatchPlan:
     """Device metadata of one ragged batch (page-padded token space).
 
@@ -84,24 +88,89 @@ class BatchPlan:
     src_tables/dst_tables (device addresses of the per-request block tables,
     int64 [R]) are set, src_blocks/dst_blocks are filled on the device by the
     step's table stage (``gather_tables``) rather than on the host.
+
+    Built either from those tensors (fields in the order above, positional or
+    by name), or -- the method's per-step path -- from one staged buffer
+    ``meta`` (int64 words ``[page_off | dst_off | round_start | semantic |
+    src_tables | dst_tables]`` then int32 words ``[tokens | page_off]``), in
+    which case the tensor views are only made when asked for.  The ``*_addr``
+    attributes are the device addresses the step descriptor takes.
     """
 
-    num_requests: int
-    total_pages: int
-    tokens: torch.Tensor
-    page_off: torch.Tensor
-    src_blocks: torch.Tensor
-    src_off: torch.Tensor
-    dst_blocks: torch.Tensor
-    dst_off: torch.Tensor
-    round_start: torch.Tensor
-    semantic: torch.Tensor
-    tokens_host: tuple[int, ...]
-    max_dst_blocks: int
-    src_tables: torch.Tensor | None = None
-    dst_tables: torch.Tensor | None = None
-    keep_alive: list | None = None  # converted block tables referenced by src/dst_tables
-    blocks_per_page: int = 1  # kernel blocks per entry of the src/dst tables (scheduler pages)
+    def __init__(self, *args, meta: torch.Tensor | None = None, n64: int = 0, with_dst: bool = True, **kw):
+        vals = dict(zip(_PLAN_FIELDS, args))
+        vals.update(kw)
+        self.num_requests = int(vals["num_requests"])
+        self.total_pages = int(vals["total_pages"])
+        self.src_blocks = vals["src_blocks"]
+        self.dst_blocks = vals["dst_blocks"]
+        self.tokens_host = tuple(vals["tokens_host"])
+        self.max_dst_blocks = int(vals["max_dst_blocks"])
+        self.keep_alive = vals.get("keep_alive")
+        self.blocks_per_page = int(vals.get("blocks_per_page", 1))
+        self.meta = meta
+        self.n64 = n64
+        R = self.num_requests
+        if meta is None:
+            self._views = {k: vals.get(k) for k in ("tokens", "page_off", "src_off", "dst_off", "round_start",
+                                                    "semantic", "src_tables", "dst_tables")}
+            ptr = lambda k: None if self._views[k] is None else self._views[k].data_ptr()
+            self.tokens_addr, self.page_off_addr = ptr("tokens"), ptr("page_off")
+            self.src_off_addr, self.dst_off_addr = ptr("src_off"), ptr("dst_off")
+            self.round_start_addr, self.semantic_addr = ptr("round_start"), ptr("semantic")
+            self.src_tables_addr, self.dst_tables_addr = ptr("src_tables"), ptr("dst_tables")
+            return
+        self._views = None
+        base = meta.data_ptr()
+        self.src_off_addr = base
+        self.dst_off_addr = base + 8 * (R + 1)
+        self.round_start_addr = base + 8 * (2 * R + 2)
+        self.semantic_addr = base + 8 * (3 * R + 2)
+        self.src_tables_addr = base + 8 * (4 * R + 2)
+        self.dst_tables_addr = base + 8 * (5 * R + 2) if with_dst else None
+        self.tokens_addr = base + 8 * n64
+        self.page_off_addr = self.tokens_addr + 4 * R
+
+    def _view(self, name: str, i64_start: int | None, i32_start: int | None, n: int) -> torch.Tensor | None:
+        if self._views is not None:
+            return self._views[name]
+        if i64_start is not None:
+            return self.meta[i64_start: i64_start + n]
+        return self.meta.view(torch.int32)[2 * self.n64 + i32_start: 2 * self.n64 + i32_start + n]
+
+    @property
+    def src_off(self) -> torch.Tensor:
+        return self._view("src_off", 0, None, self.num_requests + 1)
+
+    @property
+    def dst_off(self) -> torch.Tensor:
+        return self._view("dst_off", self.num_requests + 1, None, self.num_requests + 1)
+
+    @property
+    def round_start(self) -> torch.Tensor:
+        return self._view("round_start", 2 * self.num_requests + 2, None, self.num_requests)
+
+    @property
+    def semantic(self) -> torch.Tensor:
+        return self._view("semantic", 3 * self.num_requests + 2, None, self.num_requests)
+
+    @property
+    def src_tables(self) -> torch.Tensor | None:
+        return self._view("src_tables", 4 * self.num_requests + 2, None, self.num_requests)
+
+    @property
+    def dst_tables(self) -> torch.Tensor | None:
+        if self._views is None and self.dst_tables_addr is None:
+            return None
+        return self._view("dst_tables", 5 * self.num_requests + 2, None, self.num_requests)
+
+    @property
+    def tokens(self) -> torch.Tensor:
+        return self._view("tokens", None, 0, self.num_requests)
+
+    @property
+    def page_off(self) -> torch.Tensor:
+        return self._view("page_off", None, self.num_requests, self.num_requests + 1)
 
     @property
     def tok_total(self) -> int:

@@ -139,8 +139,8 @@ class _MetadataStager:
         self.dev_ptr = self.dev.data_ptr()
         self.cap = cap
 
-    def stage(self, i64: list[int], i32: list[int]) -> tuple[torch.Tensor, torch.Tensor]:
-        """Device views (int64 [len(i64)], int32 [len(i32)]) of the staged values."""
+    def stage(self, i64: list[int], i32: list[int]) -> torch.Tensor:
+        """Copy int64 words ``i64`` then int32 words ``i32`` to the device buffer (returned)."""
         n64 = len(i64)
         n = n64 + (len(i32) + 1) // 2
         if n > self.cap:
@@ -154,7 +154,7 @@ class _MetadataStager:
         lib, stream = N.lib(), K._stream()
         N.check(lib.kvc_copy_async(self.dev_ptr, self.host_ptr[slot], 8 * n, stream), "kvc_copy_async")
         N.check(lib.kvc_record_event(self.event_handles[slot], stream), "kvc_record_event")
-        return self.dev[:n64], self.dev.view(torch.int32)[2 * n64: 2 * n64 + len(i32)]
+        return self.dev
 
 
 class TriAttentionMethod(KVCompressionMethod):
@@ -362,7 +362,11 @@ class TriAttentionMethod(KVCompressionMethod):
         self._err = torch.zeros(1, dtype=torch.int32, device=device)
         self._err_host = torch.zeros(1, dtype=torch.int32).pin_memory()
         self._err_event = None
-        self._err_ev: torch.cuda.Event | None = None
+        # the native step copies the error word to _err_host and records this
+        # event after every selecting call, so a later call can test it cheaply
+        self._err_ev = torch.cuda.Event()
+        self._err_ev.record()  # creates the event
+        self._results: tuple | None = None
         self._strict = os.environ.get(_STRICT_ENV, "") == "1"
         self._last_shape = (0, 0, 0, 0)
         self._bind_step()
@@ -391,12 +395,14 @@ class TriAttentionMethod(KVCompressionMethod):
         plan = self._plan([(r.physical_num_tokens, r.semantic_num_tokens, r.source_block_ids_device,
                             r.destination_block_ids_device) for r in reqs], bpp=cache_blocks_per_page)
         self._run_step(plan, compact=True, stage_commit=stage_commit)
-        self._arm_error_check()
+        self._err_event = self._err_ev  # recorded by the native step behind its error read-back
         if self._strict:
             self.check_device_errors()
-        lengths = tuple((c.name, self.config.kv_budget) for c in self.materialization_caches)
-        return tuple(CompressionResult(physical_num_tokens=self.config.kv_budget,
-                                       per_layer_physical_num_tokens=lengths) for _ in reqs)
+        if self._results is None or len(self._results) < len(reqs):
+            lengths = tuple((c.name, self.config.kv_budget) for c in self.materialization_caches)
+            one = CompressionResult(physical_num_tokens=self.config.kv_budget, per_layer_physical_num_tokens=lengths)
+            self._results = (one,) * max(len(reqs), 2 * len(self._results or ()))  # immutable: shared
+        return self._results[: len(reqs)]
 
     def select_many(self, requests: Sequence[CompressionRequest], *, cache_blocks_per_page: int = 1
                     ) -> torch.Tensor:
@@ -561,12 +567,14 @@ class TriAttentionMethod(KVCompressionMethod):
         """
         budget = self.config.kv_budget
         bs = self.cache_block_size
-        dev = self.offsets.device
+        dev_index = self.offsets.get_device()
+        i64_t = torch.int64
         if isinstance(bpp, bool) or not isinstance(bpp, int) or bpp < 1:
             raise ValueError("cache_blocks_per_page must be a positive integer")
         tokens, sem, src_ptrs, dst_ptrs, keep_alive = [], [], [], [], []
         page_off = [0]
         dst_need = -(-budget // bs)
+        dst_min = -(-dst_need // bpp)
         for t, s, src, dst in items:
             t, s = int(t), int(s)
             if budget <= 0 or budget > t:
@@ -574,34 +582,31 @@ class TriAttentionMethod(KVCompressionMethod):
             n = -(-t // bs)
             if src.numel() < -(-n // bpp):
                 raise RuntimeError("source block table is shorter than the physical token count")
-            if src.dtype != torch.int64 or src.device != dev or not src.is_contiguous():
-                src = src.to(device=dev, dtype=torch.int64).contiguous()
+            if src.dtype is not i64_t or src.get_device() != dev_index or not src.is_contiguous():
+                src = src.to(device=self.offsets.device, dtype=i64_t).contiguous()
                 keep_alive.append(src)
             tokens.append(t)
             page_off.append(page_off[-1] + n)
             sem.append(s)
             src_ptrs.append(src.data_ptr())
             if need_destination:
-                if dst is None or dst.numel() < -(-dst_need // bpp):
+                if dst is None or dst.numel() < dst_min:
                     raise RuntimeError("destination block table is shorter than kv_budget")
-                if dst.dtype != torch.int64 or dst.device != dev or not dst.is_contiguous():
-                    dst = dst.to(device=dev, dtype=torch.int64).contiguous()
+                if dst.dtype is not i64_t or dst.get_device() != dev_index or not dst.is_contiguous():
+                    dst = dst.to(device=self.offsets.device, dtype=i64_t).contiguous()
                     keep_alive.append(dst)
                 dst_ptrs.append(dst.data_ptr())
         R = len(tokens)
         dst_off = list(range(0, (R + 1) * dst_need, dst_need)) if need_destination else [0] * (R + 1)
-        i64, i32 = self._stager.stage(page_off + dst_off + sem + sem + src_ptrs + dst_ptrs, tokens + page_off)
+        i64 = page_off + dst_off + sem + sem + src_ptrs + dst_ptrs
+        meta = self._stager.stage(i64, tokens + page_off)
         ws = self._ws
-        src_blocks = ws.get("src_blocks", page_off[-1], torch.int64)
-        dst_blocks = ws.get("dst_blocks", R * dst_need, torch.int64) if need_destination else src_blocks[:0]
-        q = 4 * R + 2
-        return K.BatchPlan(
-            num_requests=R, total_pages=page_off[-1], tokens=i32[:R], page_off=i32[R:],
-            src_blocks=src_blocks, src_off=i64[: R + 1], dst_blocks=dst_blocks, dst_off=i64[R + 1: 2 * R + 2],
-            round_start=i64[2 * R + 2: 3 * R + 2], semantic=i64[3 * R + 2: q], tokens_host=tuple(tokens),
-            max_dst_blocks=dst_need, src_tables=i64[q: q + R],
-            dst_tables=i64[q + R: q + 2 * R] if need_destination else None, keep_alive=keep_alive,
-            blocks_per_page=bpp)
+        src_blocks = ws.get("src_blocks", page_off[-1], i64_t)
+        dst_blocks = ws.get("dst_blocks", R * dst_need, i64_t) if need_destination else src_blocks[:0]
+        return K.BatchPlan(num_requests=R, total_pages=page_off[-1], meta=meta, n64=len(i64),
+                           src_blocks=src_blocks, dst_blocks=dst_blocks, tokens_host=tuple(tokens),
+                           max_dst_blocks=dst_need, with_dst=need_destination, keep_alive=keep_alive,
+                           blocks_per_page=bpp)
 
     def _mark(self, name: str) -> None:
         if self.profiler is not None:
@@ -645,10 +650,12 @@ class TriAttentionMethod(KVCompressionMethod):
         st.extra = self.scoring_extra.data_ptr()
         st.q_pass_t = K._p(self.scoring_q_pass_t)
         st.error_flag = self._err.data_ptr()
+        st.error_host = self._err_host.data_ptr()
+        st.error_event = self._err_ev.cuda_event
         self._step = st
         self._step_ref = ctypes.byref(st)
 
-    def _launch(self, stages: int, slots) -> None:
+    def _launch(self, stages: int, slots, exchange: bool = False) -> None:
         """kvc_triattention_run on the current stream (with stage events when profiled)."""
         events = None
         prof = self.profiler
@@ -658,7 +665,7 @@ class TriAttentionMethod(KVCompressionMethod):
                 ev = torch.cuda.Event(enable_timing=True)
                 ev.record()  # creates the event; the library records it again at its stage boundary
                 events[i] = ev.cuda_event
-                prof.add(N.STEP_EVENT_NAMES[i], ev)
+                prof.add("tp_sync" if exchange and i == 4 else N.STEP_EVENT_NAMES[i], ev)
         N.check(N.lib().kvc_triattention_run(self._step_ref, stages, events, K._stream()), "kvc_triattention_run")
 
     def _set_plan(self, plan: K.BatchPlan) -> N.TriAttentionStep:
@@ -666,16 +673,16 @@ class TriAttentionMethod(KVCompressionMethod):
         st = self._step
         st.num_requests = plan.num_requests
         st.total_pages = plan.total_pages
-        st.tokens = plan.tokens.data_ptr()
-        st.page_off = plan.page_off.data_ptr()
+        st.tokens = plan.tokens_addr
+        st.page_off = plan.page_off_addr
         st.src_blocks = plan.src_blocks.data_ptr()
-        st.src_block_off = plan.src_off.data_ptr()
+        st.src_block_off = plan.src_off_addr
         st.dst_blocks = plan.dst_blocks.data_ptr()
-        st.dst_block_off = plan.dst_off.data_ptr()
-        st.round_start = plan.round_start.data_ptr()
-        st.semantic = plan.semantic.data_ptr()
-        st.src_tables = plan.src_tables.data_ptr()
-        st.dst_tables = K._p(plan.dst_tables)
+        st.dst_block_off = plan.dst_off_addr
+        st.round_start = plan.round_start_addr
+        st.semantic = plan.semantic_addr
+        st.src_tables = plan.src_tables_addr
+        st.dst_tables = plan.dst_tables_addr
         st.cache_blocks_per_page = plan.blocks_per_page
         return st
 
@@ -721,17 +728,18 @@ class TriAttentionMethod(KVCompressionMethod):
         ex = self._peer
         if ex is not None:
             # rows go straight into the peer-mapped exchange buffer; the exchange
-            # kernel replaces the all-reduce and the layer reduction
+            # kernel replaces the all-reduce and the layer reduction, inside the
+            # same native call as the other stages
             ex.ensure(L, tok)
             st.rows = ex.rows_ptr
             st.agg = ex.agg_ptr
-            self._launch(head, (0, 1, 2, 3))
-            self._mark("tp_sync")
-            ex.exchange(L, plan.total_pages, plan.tokens, plan.page_off, R, self.layer_aggregation_code, self._err,
-                        K._stream())
+            st.peer_rows, st.peer_agg, st.peer_flags = ex.tables()
+            st.world, st.rank = ex.world, ex.rank
+            st.epoch = ex.next_epoch()
+            stages = head | N.STAGE_EXCHANGE | (tail & ~N.STAGE_AGGREGATE)
+            self._launch(stages, (0, 1, 2, 3, *tail_slots), exchange=True)
             if self.profiler is not None and hasattr(self.profiler, "exchange_done"):
                 self.profiler.exchange_done(ex)
-            self._launch(tail & ~N.STAGE_AGGREGATE, tail_slots[1:])
         elif self.tensor_parallel_size > 1:
             self._launch(head, (0, 1, 2, 3))
             self._mark("tp_sync")
@@ -765,17 +773,6 @@ class TriAttentionMethod(KVCompressionMethod):
         return "peer" if self._peer is not None else "nccl"
 
     # ---- device error reporting ---------------------------------------------
-
-    def _arm_error_check(self) -> None:
-        """Queue the error word's read-back and an event behind it (checked at the next call)."""
-        if self._err_ev is None:
-            self._err_ev = torch.cuda.Event()
-            self._err_ev.record()  # creates the event
-            self._err_ev_handle = self._err_ev.cuda_event
-        lib, stream = N.lib(), K._stream()
-        N.check(lib.kvc_copy_async(self._err_host.data_ptr(), self._err.data_ptr(), 4, stream), "kvc_copy_async")
-        N.check(lib.kvc_record_event(self._err_ev_handle, stream), "kvc_record_event")
-        self._err_event = self._err_ev
 
     def _raise_pending_device_error(self) -> None:
         ev = self._err_event

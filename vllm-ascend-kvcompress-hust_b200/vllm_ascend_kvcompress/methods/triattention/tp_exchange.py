@@ -142,15 +142,23 @@ class PeerScoreExchange:
         w = int(N.lib().kvc_tp_exchange_stamp_word(self.world))
         return self.buf[4 * w: 4 * w + 32].view(torch.int64)
 
-    def exchange(self, layers: int, total_pages: int, tokens: torch.Tensor, page_off: torch.Tensor,
-                 num_requests: int, layer_aggregation: int, error_flag: torch.Tensor, stream: int) -> None:
-        """Queue this rank's share of the step's sync on ``stream`` (all ranks call it each step)."""
-        self.epoch += 1
+    def tables(self) -> tuple[int, int, int]:
+        """Device addresses of the rows, agg and flags tables (``world`` addresses each)."""
         t = self.table.data_ptr()
-        w = self.world
-        N.check(N.lib().kvc_tp_exchange_max(t, t + 8 * w, t + 16 * w, w, self.rank, layers, total_pages,
-                                            tokens.data_ptr(), page_off.data_ptr(), num_requests, layer_aggregation,
-                                            self.epoch, error_flag.data_ptr(), stream), "kvc_tp_exchange_max")
+        return t, t + 8 * self.world, t + 16 * self.world
+
+    def next_epoch(self) -> int:
+        """The epoch of the next exchange (every rank advances it once per step)."""
+        self.epoch += 1
+        return self.epoch
+
+    def exchange(self, layers: int, total_pages: int, tokens: int, page_off: int, num_requests: int,
+                 layer_aggregation: int, error_flag: int, stream: int) -> None:
+        """Queue this rank's share of a sync on ``stream`` as a call of its own (all ranks call it)."""
+        rows, agg, flags = self.tables()
+        N.check(N.lib().kvc_tp_exchange_max(rows, agg, flags, self.world, self.rank, layers, total_pages, tokens,
+                                            page_off, num_requests, layer_aggregation, self.next_epoch(),
+                                            error_flag, stream), "kvc_tp_exchange_max")
 
     def close(self) -> None:
         """Unmap the other ranks' buffers (callers synchronise first); this rank's buffer stays."""
