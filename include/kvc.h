@@ -360,36 +360,50 @@ int kvc_stage_commit(const int64_t* dst_blocks, const int64_t* dst_block_off, in
  * and the sum/amax, division and nan_to_num that follow,
  * methods/triattention/method.py:447-467).
  *
- * Every rank of the TP group calls it once per step on its stream, with the
- * same world, layers, pages, requests and epoch.  peer_rows[p] is rank p's
- * rows buffer ([L][total_pages*128] fp32, the kvc_normalize_aggregate rows of
- * its local heads), peer_agg[p] its agg buffer ([total_pages*128]) and
- * peer_flags[p] its flag words (kvc_tp_exchange_flag_words(world) int32,
- * zero-initialised once); the three are device arrays of `world` device
- * addresses valid on this GPU (this rank's own buffers at index `rank`, the
- * others mapped with kvc_ipc_open); every rows/agg buffer 16-byte aligned
- * (the kernel moves 4 tokens per access).  On return (stream order) every rank's
- * agg holds the finalised scores of the whole step: the max over ranks of each
- * layer's row (NaN-propagating), reduced over layers (sequential sum then / L,
- * or max) and mapped NaN -> -inf, +inf -> 1e30; page padding is 0.  This is
- * bit-identical to kvc_aggregate_rows applied to the TP=1 rows.
- * epoch: a positive step counter, one larger on every call (flags are never
+ * The step's tokens are split into `world` equal ranges of 4-token quads
+ * (kvc_tp_exchange_inbox_floats gives the sizes); rank o owns range o.  Every
+ * rank of the TP group calls, once per step and on its stream, with the same
+ * world, layers, pages, requests and epoch:
+ *   kvc_tp_push_rows     after kvc_head_stats, in place of
+ *                        kvc_normalize_aggregate: normalises its local heads'
+ *                        raw scores and stores each quad's head max per layer
+ *                        into the owning rank's inbox (plain peer stores);
+ *   kvc_tp_exchange_max  before the selection: reduces the owned quads from
+ *                        its own inbox (max over ranks, NaN-propagating), reduces
+ *                        the layers (sequential sum then / L, or max),
+ *                        finalises (NaN -> -inf, +inf -> 1e30; page padding 0)
+ *                        and stores the scores into every rank's agg buffer.
+ * On return (stream order) every rank's agg holds the finalised scores of the
+ * whole step, bit-identical to kvc_normalize_aggregate + kvc_aggregate_rows of
+ * the TP = 1 rows.  peer_inbox[p] is rank p's inbox
+ * (kvc_tp_exchange_inbox_floats(world, L, total_pages) fp32, layout
+ * [world source ranks][L][quads per rank][4]), peer_agg[p] its agg buffer
+ * ([total_pages*128] fp32) and peer_flags[p] its flag words
+ * (kvc_tp_exchange_flag_words(world) int32, zero-initialised once); the three
+ * are device arrays of `world` device addresses valid on this GPU (this rank's
+ * own buffers at index `rank`, the others mapped with kvc_ipc_open); every
+ * inbox/agg buffer 16-byte aligned.
+ * epoch: a positive step counter, one larger on every step (flags are never
  * cleared).  Waits for other ranks are bounded (2 s); on expiry the kernel
- * raises KVC_DEV_TIMEOUT in error_flag and completes.  One kernel launch per
- * call; when it completes on this rank's stream every rank has finished
- * reading this rank's rows, so the next step's normalisation may rewrite them.
- * num_layers <= 512.
- * Flag words (kvc_tp_exchange_flag_words): ready[world], pushed[world], a CTA
- * counter, the started epoch, then from word kvc_tp_exchange_stamp_word(world)
+ * raises KVC_DEV_TIMEOUT in error_flag and completes.  When the exchange has
+ * completed on this rank's stream every rank has finished reading its inbox,
+ * so the next step's pushes may arrive.  num_layers <= 512.
+ * Flag words: delivered[world], pushed[world], two CTA counters, the started
+ * epoch, a spare word, then from word kvc_tp_exchange_stamp_word(world)
  * (8-byte aligned when the flags are) four uint64 %globaltimer stamps of this
- * rank's last step: first CTA start, first CTA to see every rank ready, last
- * CTA done, every rank's scores pushed.  Stamp 1 - stamp 0 is the wait for the
- * slowest rank; stamp 3 - stamp 1 the exchange itself.
+ * rank's last exchange: first CTA start, first CTA to see every rank's rows
+ * delivered, last CTA done, every rank's scores pushed.  Stamp 1 - stamp 0 is
+ * the wait for the slowest rank; stamp 3 - stamp 1 the exchange itself.
  */
 #define KVC_TP_MAX_WORLD 64
 int kvc_tp_exchange_flag_words(int world);
 int kvc_tp_exchange_stamp_word(int world);
-int kvc_tp_exchange_max(const float* const* peer_rows, float* const* peer_agg, int32_t* const* peer_flags,
+int64_t kvc_tp_exchange_inbox_floats(int world, int num_layers, int total_pages);
+int kvc_tp_push_rows(const float* raw, int num_layers, int heads, int total_pages, const float* mean,
+                     const float* denom, const int32_t* tokens, const int32_t* page_off, int num_requests,
+                     float* const* peer_inbox, int32_t* const* peer_flags, int world, int rank, int32_t epoch,
+                     void* stream);
+int kvc_tp_exchange_max(float* const* peer_inbox, float* const* peer_agg, int32_t* const* peer_flags,
                         int world, int rank, int num_layers, int total_pages, const int32_t* tokens,
                         const int32_t* page_off, int num_requests, int layer_aggregation, int32_t epoch,
                         int32_t* error_flag, void* stream);
@@ -442,10 +456,12 @@ int kvc_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
  *   KVC_STAGE_AGGREGATE layer reduction into agg (kvc_aggregate_rows)
  *   KVC_STAGE_SELECT    kvc_select_keep into keep
  *   KVC_STAGE_COMPACT   kvc_compact (+ commit staging when staged_rows/offsets)
- *   KVC_STAGE_EXCHANGE  the tensor-parallel peer score sync: kvc_tp_exchange_max
- *                       with peer_rows / peer_agg / peer_flags, world, rank
- *                       and epoch (rows and agg must be this rank's buffers
- *                       of the exchange); not together with AGGREGATE
+ *   KVC_STAGE_EXCHANGE  the tensor-parallel peer score sync with peer_inbox /
+ *                       peer_agg / peer_flags, world, rank and epoch: the
+ *                       SCORE stage's normalisation becomes kvc_tp_push_rows
+ *                       and kvc_tp_exchange_max follows it (agg must be this
+ *                       rank's agg buffer of the exchange); not together with
+ *                       AGGREGATE
  * A tensor-parallel caller with the peer exchange runs TABLES | SCORE |
  * EXCHANGE | SELECT | COMPACT in one call; with an NCCL all-reduce instead it
  * runs TABLES | SCORE, all-reduces rows with MAX, then AGGREGATE | SELECT | COMPACT.
@@ -539,7 +555,7 @@ typedef struct kvc_triattention_step {
   int32_t* error_host;
   void* error_event;
   /* KVC_STAGE_EXCHANGE: device arrays of `world` addresses (this rank's at `rank`) */
-  const float* const* peer_rows;
+  float* const* peer_inbox;
   float* const* peer_agg;
   int32_t* const* peer_flags;
   int32_t world;

@@ -129,8 +129,10 @@ def test_step_rejects_bad_stage_masks_without_launch():
 def test_exchange_ipc_and_unrotate_validate_on_the_host():
     lib = N.lib()
     fake = ctypes.c_void_p(0x1000)
-    assert lib.kvc_tp_exchange_flag_words(8) == 26 and lib.kvc_tp_exchange_flag_words(0) == 0
-    assert lib.kvc_tp_exchange_stamp_word(8) == 18 and lib.kvc_tp_exchange_stamp_word(8) % 2 == 0
+    assert lib.kvc_tp_exchange_flag_words(8) == 28 and lib.kvc_tp_exchange_flag_words(0) == 0
+    assert lib.kvc_tp_exchange_stamp_word(8) == 20 and lib.kvc_tp_exchange_stamp_word(8) % 2 == 0
+    # inbox: 8 sources x 6 layers x ceil(1000 pages * 32 quads / 8) quads x 4 floats
+    assert lib.kvc_tp_exchange_inbox_floats(8, 6, 1000) == 8 * 6 * 4000 * 4
     # exchange: NULL tables, rank outside the world, world above the maximum, epoch 0, bad aggregation
     assert lib.kvc_tp_exchange_max(None, fake, fake, 2, 0, 1, 1, fake, fake, 1, 0, 1, None, None) == -14
     assert lib.kvc_tp_exchange_max(fake, fake, fake, 2, 2, 1, 1, fake, fake, 1, 0, 1, None, None) == -22

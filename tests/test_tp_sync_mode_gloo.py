@@ -51,9 +51,10 @@ def test_exchange_layout_is_aligned_and_ordered():
     sys.path.insert(0, str(ROOT / "vllm-ascend-kvcompress-hust_b200"))
     from vllm_ascend_kvcompress.methods.triattention.tp_exchange import exchange_layout
 
-    flags, agg, rows, total = exchange_layout(8, 6, 1000, 17)
-    assert flags == 0 and agg == 256 and rows == 256 + 4096 and total == rows + 24064
-    assert all(x % 256 == 0 for x in (agg, rows, total))
+    flags, agg, inbox, total = exchange_layout(8, 6, 1000, 26)
+    # 250 quads over 8 ranks -> 32 per rank; inbox 8 sources x 6 layers x 32 quads x 16 B
+    assert flags == 0 and agg == 256 and inbox == 256 + 4096 and total == inbox + 8 * 6 * 32 * 16
+    assert all(x % 256 == 0 for x in (agg, inbox, total))
 
 
 def test_exchange_buffers_grow_collectively_only_when_needed(monkeypatch):

@@ -16,6 +16,7 @@
 // per-request phase (c, sn) into a and b once per (request, layer) leaves three
 // FMAs per (token, q head, frequency) in the streaming loop.
 #include "kvc_common.cuh"
+#include "kvc_norm.cuh"
 
 namespace kvc {
 
@@ -461,103 +462,27 @@ __global__ void __launch_bounds__(1024) head_stats_kernel(const float* __restric
 // normalisation, head max, layer aggregation
 // --------------------------------------------------------------------------
 
-// a / b from the correctly rounded reciprocal rcp = RN(1/b): q0 = RN(a * rcp),
-// residual r = a - q0 * b (exact by FMA), q = RN(q0 + r * rcp).  Markstein's
-// correction step (P. Markstein, "Computation of elementary functions on the
-// IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990) returns the
-// correctly rounded quotient for normal operands, as IEEE division would; the
-// denominators here are >= 1e-3 and the numerators finite or NaN/inf, which
-// propagate the same way.  Falls back to the division when a, b are not finite.
-__device__ __forceinline__ float div_by(float a, float b, float rcp) {
-  if (!isfinite(a) || !isfinite(b)) return __fdiv_rn(a, b);
-  const float q0 = __fmul_rn(a, rcp);
-  const float r = __fmaf_rn(-q0, b, a);
-  return __fmaf_rn(r, rcp, q0);
-}
-
-// Grid (1024-token blocks, scoring layers): one thread per (4 consecutive
-// tokens, layer), loading each query head's raw scores of its 4 tokens as one
-// 16-byte vector (page-major raw: a page's 128 scores of one head are
-// contiguous).  A CTA covers 8 pages; the request of each page and its
-// per-head mean, denominator and reciprocal for this layer are staged in
-// shared memory first.  The thread writes the layer's head-max row for its 4
-// tokens; aggregate_rows then reduces the layers (the same path serves TP=1
-// and the TP sync).
-constexpr int kNormPages = 8;  // pages per CTA (256 threads x 4 tokens)
-
+// Grid (8-page blocks, scoring layers): one thread per (4 consecutive tokens,
+// layer) computes the head max of the normalised scores (kvc_norm.cuh) and
+// writes the layer's row; aggregate_rows then reduces the layers (TP = 1 and
+// the NCCL sync).  Page padding is written as 0, keeping rows finite for the
+// MAX sync.
 __global__ void __launch_bounds__(256) normalize_kernel(const float* __restrict__ raw, int L, int heads,
                                                         int total_pages, const float* __restrict__ mean,
                                                         const float* __restrict__ den,
                                                         const int32_t* __restrict__ tokens,
                                                         const int32_t* __restrict__ page_off, int R,
                                                         float* rows) {
-  extern __shared__ float st[];  // [kNormPages][heads] mean, den, 1/den
-  __shared__ int req_s[kNormPages];
-  __shared__ int64_t start_s[kNormPages];
-  __shared__ int ntok_s[kNormPages];
+  extern __shared__ float st[];  // [3][kNormPages][heads]
+  __shared__ NormPages np;
   const int l = blockIdx.y;
   const int page0 = blockIdx.x * kNormPages;
-  if (threadIdx.x < kNormPages) {
-    const int p = page0 + threadIdx.x;
-    int r = 0;
-    if (p < total_pages) {
-      r = request_of_page(page_off, R, p);
-      start_s[threadIdx.x] = (int64_t)__ldg(page_off + r) * kBlock;
-      ntok_s[threadIdx.x] = __ldg(tokens + r);
-    }
-    req_s[threadIdx.x] = r;
-  }
-  __syncthreads();
-  float* mu_s = st;
-  float* dn_s = st + kNormPages * heads;
-  float* rc_s = st + 2 * kNormPages * heads;
-  for (int i = threadIdx.x; i < kNormPages * heads; i += blockDim.x) {
-    const int slot = i / heads;
-    if (page0 + slot >= total_pages) continue;
-    const int64_t g = ((int64_t)l * R + req_s[slot]) * heads + i % heads;
-    mu_s[i] = __ldg(mean + g);
-    const float d = __ldg(den + g);
-    dn_s[i] = d;
-    rc_s[i] = __frcp_rn(d);
-  }
-  __syncthreads();
-  const int slot = threadIdx.x >> 5;  // 32 threads x 4 tokens per page
-  const int p = page0 + slot;
-  if (p >= total_pages) return;
-  const int64_t tok_total = (int64_t)total_pages * kBlock;
-  const int64_t tok = (int64_t)p * kBlock + (threadIdx.x & 31) * 4;
-  const int t = (int)(tok - start_s[slot]);
-  const int n = ntok_s[slot];
-  float4* out = reinterpret_cast<float4*>(rows + (int64_t)l * tok_total + tok);
-  if (t >= n) {  // page padding: keep rows finite for the MAX sync
-    *out = make_float4(0.f, 0.f, 0.f, 0.f);
-    return;
-  }
-  const float* mu = mu_s + slot * heads;
-  const float* dn = dn_s + slot * heads;
-  const float* rc = rc_s + slot * heads;
-  const float4* rl = reinterpret_cast<const float4*>(raw + ((int64_t)l * total_pages + p) * heads * kBlock +
-                                                     (tok & (kBlock - 1)));
-  constexpr int U = 4;  // heads whose loads are in flight together (16 floats per thread)
-  float4 z = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-  for (int h0 = 0; h0 < heads; h0 += U) {
-    float4 x[U];
-#pragma unroll
-    for (int k = 0; k < U; ++k)
-      if (h0 + k < heads) x[k] = __ldg(rl + (int64_t)(h0 + k) * (kBlock / 4));
-#pragma unroll
-    for (int k = 0; k < U; ++k) {
-      const int h = h0 + k;
-      if (h < heads) {
-        const float m = mu[h], d = dn[h], c = rc[h];
-        z.x = nan_max(z.x, div_by(x[k].x - m, d, c));
-        z.y = nan_max(z.y, div_by(x[k].y - m, d, c));
-        z.z = nan_max(z.z, div_by(x[k].z - m, d, c));
-        z.w = nan_max(z.w, div_by(x[k].w - m, d, c));
-      }
-    }
-  }
-  *out = make_float4(t + 0 < n ? z.x : 0.f, t + 1 < n ? z.y : 0.f, t + 2 < n ? z.z : 0.f, t + 3 < n ? z.w : 0.f);
+  norm_stage(np, st, page0, l, heads, total_pages, R, tokens, page_off, mean, den);
+  if (page0 + (int)(threadIdx.x >> 5) >= total_pages) return;
+  int64_t tok;
+  float4 z;
+  norm_quad(np, st, raw, l, heads, total_pages, page0, tok, z);
+  *reinterpret_cast<float4*>(rows + (int64_t)l * total_pages * kBlock + tok) = z;
 }
 
 __global__ void __launch_bounds__(256) aggregate_rows_kernel(const float* __restrict__ rows, int L,

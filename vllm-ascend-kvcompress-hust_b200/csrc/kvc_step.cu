@@ -52,7 +52,9 @@ inline void mark(void* const* events, int slot, cudaStream_t st) {
   if (events && events[slot]) cudaEventRecord((cudaEvent_t)events[slot], st);
 }
 
-int score_stage(const kvc_triattention_step& s, void* const* ev, void* stream) {
+// push: the peer exchange follows, so normalisation delivers each quad's head
+// max to the inbox of the rank that owns it instead of writing local rows.
+int score_stage(const kvc_triattention_step& s, void* const* ev, void* stream, bool push) {
   cudaStream_t st = (cudaStream_t)stream;
   const int F = s.rotary_dim / 2;
   const int P = s.head_dim - s.rotary_dim;
@@ -89,6 +91,11 @@ int score_stage(const kvc_triattention_step& s, void* const* ev, void* stream) {
                       s.mean, s.var, s.den, stream);
   if (rc != KVC_OK) return rc;
   mark(ev, 3, st);
+  if (push) {
+    KVC_CHECK_ARG(s.peer_inbox && s.peer_flags, KVC_ENULL);
+    return kvc_tp_push_rows(s.raw, s.score_layers, heads, s.total_pages, s.mean, s.den, s.tokens, s.page_off,
+                            s.num_requests, s.peer_inbox, s.peer_flags, s.world, s.rank, s.epoch, stream);
+  }
   return kvc_normalize_aggregate(s.raw, s.score_layers, heads, s.total_pages, s.mean, s.den, s.tokens, s.page_off,
                                  s.num_requests, s.layer_aggregation, s.rows, nullptr, stream);
 }
@@ -120,7 +127,7 @@ extern "C" int kvc_triattention_run(const kvc_triattention_step* step, int stage
     if (rc != KVC_OK) return rc;
   }
   if (stages & KVC_STAGE_SCORE) {
-    rc = score_stage(s, ev, stream);
+    rc = score_stage(s, ev, stream, (stages & KVC_STAGE_EXCHANGE) != 0);
     if (rc != KVC_OK) return rc;
   }
   if (stages & KVC_STAGE_AGGREGATE) {
@@ -131,8 +138,8 @@ extern "C" int kvc_triattention_run(const kvc_triattention_step* step, int stage
   }
   if (stages & KVC_STAGE_EXCHANGE) {
     mark(ev, 4, st);
-    KVC_CHECK_ARG(s.peer_rows && s.peer_agg && s.peer_flags, KVC_ENULL);
-    rc = kvc_tp_exchange_max(s.peer_rows, s.peer_agg, s.peer_flags, s.world, s.rank, s.score_layers,
+    KVC_CHECK_ARG(s.peer_inbox && s.peer_agg && s.peer_flags, KVC_ENULL);
+    rc = kvc_tp_exchange_max(s.peer_inbox, s.peer_agg, s.peer_flags, s.world, s.rank, s.score_layers,
                              s.total_pages, s.tokens, s.page_off, s.num_requests, s.layer_aggregation, s.epoch,
                              s.error_flag, stream);
     if (rc != KVC_OK) return rc;

@@ -1,44 +1,47 @@
 // Tensor-parallel score sync over NVLink peer memory (sm_100a).
 //
-// Every TP rank holds the per-layer head-max rows of its own KV heads,
-// rows[l][tok] (the normalisation output), in a buffer the other ranks have
-// mapped through CUDA IPC.  One kernel per rank replaces the MAX all-reduce
-// and the layer reduction that follows it:
+// Every TP rank scores its own KV heads.  The step's tokens are split into
+// world equal ranges of 4-token quads; rank o "owns" range o and keeps an
+// inbox [world source ranks][L layers][per quads][4] fp32 that every other
+// rank has mapped through CUDA IPC.  Two kernels per rank replace the MAX
+// all-reduce of the per-layer rows and the layer reduction after it:
 //
-//   1. the first CTA to start signals "rows ready" to every rank (the rows are
-//      complete: the previous kernel on the stream wrote them); every CTA waits
-//      for every rank's signal;
-//   2. the rank owns 1/world of the step's tokens, in 4-token quads.  A CTA
-//      takes a group of Q quads with L/ceil(L/64) threads per quad, so each
-//      thread loads one (quad, layer) from every rank over NVLink (all loads of
-//      a group in flight at once) and keeps their NaN-propagating max in
-//      shared memory; one thread per quad then reduces the layers in order
-//      (sequential fp32 sum / L, or max) and finalises exactly as
-//      kvc_aggregate_rows does;
-//   3. the CTA stores the finished quads into every rank's agg buffer (plain
-//      peer stores, consecutive threads on consecutive quads), fences, and the
-//      last CTA signals "agg pushed" to every rank, then waits for every rank's
-//      "agg pushed" before the kernel ends, so the selection launched next on
-//      the stream reads complete scores and no rank is still reading this
-//      rank's rows when the next step's normalisation rewrites them.
+//   push (kvc_tp_push_rows): normalisation and head max of this rank's heads
+//     (the same arithmetic as kvc_normalize_aggregate, kvc_norm.cuh), each
+//     quad's value stored straight into its owner's inbox -- plain peer
+//     stores, so the NVLink traffic is writes issued while the kernel still
+//     streams raw scores from HBM.  The last CTA signals "delivered" to every
+//     rank.
+//   exchange (kvc_tp_exchange_max): every CTA waits for every rank's
+//     "delivered"; for its owned quads a CTA takes a group of Q quads with up
+//     to 64 threads per quad, one per layer, each loading the world sources of
+//     one (quad, layer) from the LOCAL inbox and keeping their NaN-propagating
+//     max in shared memory; one thread per quad reduces the layers in order
+//     (sequential fp32 sum / L, or max) and finalises exactly as
+//     kvc_aggregate_rows does; consecutive threads store consecutive finished
+//     quads into every rank's agg buffer.  The last CTA signals "agg pushed" to
+//     every rank and waits for every rank's "agg pushed" before the kernel
+//     ends, so the selection launched next reads complete scores, and no rank
+//     still reads its inbox when the next step's pushes arrive.
 //
-// Bytes over NVLink per rank: (world-1)/world of the rows (reduce) plus
-// (world-1)/world of agg (broadcast), against 2(world-1)/world of the rows for
-// a ring all-reduce.  Flags are per-step epochs (monotonic, never reset, wrap
-// safe), so no clearing pass is needed.  Every wait is bounded (2 s of
-// %globaltimer); on expiry the kernel raises KVC_DEV_TIMEOUT in the error flag
-// and completes.  The grid never exceeds one wave of resident CTAs.
+// Bytes over NVLink per rank: (world-1)/world of its rows and (world-1)/world
+// of the finished scores, all as stores.  Flags are per-step epochs
+// (monotonic, never reset, wrap safe), so no clearing pass is needed.  Every
+// wait is bounded (2 s of %globaltimer); on expiry the kernel raises
+// KVC_DEV_TIMEOUT in the error flag and completes.  The exchange grid never
+// exceeds one wave of resident CTAs.
 //
-// Flag words of one rank: ready[world], pushed[world], CTA counter, started
-// epoch, then four uint64 %globaltimer stamps of the last step on this rank:
-// first CTA start, first CTA to see every rank ready, last CTA done, every
-// rank's "agg pushed" seen (rank skew = stamp1 - stamp0, exchange = stamp3 - stamp1).
+// Flag words of one rank: delivered[world], pushed[world], exchange CTA
+// counter, started epoch, push CTA counter, one spare, then four uint64
+// %globaltimer stamps of the last exchange on this rank: first CTA start,
+// first CTA to see every rank's rows delivered, last CTA done, every rank's
+// "agg pushed" seen (rank skew = stamp1 - stamp0, exchange = stamp3 - stamp1).
 #include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <cstring>
 
-#include "kvc_common.cuh"
+#include "kvc_norm.cuh"
 
 namespace kvc {
 
@@ -46,19 +49,28 @@ constexpr uint64_t kTpWaitNs = 2000000000ull;
 constexpr int kTpThreads = 256;
 constexpr int kTpMaxLayers = 512;
 
+__host__ __device__ constexpr int tp_exch_counter(int world) { return 2 * world; }
+__host__ __device__ constexpr int tp_started(int world) { return 2 * world + 1; }
+__host__ __device__ constexpr int tp_push_counter(int world) { return 2 * world + 2; }
+__host__ __device__ constexpr int tp_stamp_word(int world) { return 2 * world + 4; }
+
+// Quads of the padded token space owned by each rank.
+__host__ __device__ inline int64_t tp_quads_per_rank(int64_t tok_total, int world) {
+  return (tok_total / 4 + world - 1) / world;
+}
+
 struct TpArgs {
-  const float* const* rows;  // [world] each rank's rows[L][tok_total]
+  float* const* inbox;       // [world] each rank's inbox [world][L][per][4]
   float* const* agg;         // [world] each rank's agg[tok_total]
   int32_t* const* flags;     // [world] each rank's flag words
   const int32_t* tokens;
   const int32_t* page_off;
   int32_t* error_flag;
   int64_t tok_total;
+  int64_t per;               // quads per owner
   int world, rank, L, R, layer_agg;
   int32_t epoch;
 };
-
-__host__ __device__ constexpr int tp_stamp_word(int world) { return 2 * world + 2; }
 
 __device__ __forceinline__ uint64_t tp_now_ns() {
   uint64_t t;
@@ -94,34 +106,73 @@ __device__ __forceinline__ float4 nan_max4(float4 a, float4 b) {
 }
 
 // Valid tokens (0..4) of the quad starting at token `tok` of the page-padded space.
-__device__ __forceinline__ int quad_valid(const TpArgs& a, int64_t tok) {
-  const int r = request_of_page(a.page_off, a.R, (int)(tok >> 7));
-  const int t = (int)(tok - (int64_t)__ldg(a.page_off + r) * kBlock);
-  return max(0, min(4, __ldg(a.tokens + r) - t));
+__device__ __forceinline__ int quad_valid(const int32_t* page_off, const int32_t* tokens, int R, int64_t tok) {
+  const int r = request_of_page(page_off, R, (int)(tok >> 7));
+  const int t = (int)(tok - (int64_t)__ldg(page_off + r) * kBlock);
+  return max(0, min(4, __ldg(tokens + r) - t));
 }
 
-// W: the world size when it is compiled in (1, 2, 4, 8), else 0 (runtime, loads in groups of 8).
+// ---- push: normalise this rank's heads and deliver each quad to its owner ----
+
+struct PushArgs {
+  const float* raw;
+  const float* mean;
+  const float* den;
+  const int32_t* tokens;
+  const int32_t* page_off;
+  float* const* inbox;
+  int32_t* const* flags;
+  int64_t per;
+  int L, heads, total_pages, R, world, rank;
+  int32_t epoch;
+};
+
+__global__ void __launch_bounds__(256) tp_push_rows_kernel(const __grid_constant__ PushArgs a) {
+  extern __shared__ float st[];  // [3][kNormPages][heads]
+  __shared__ NormPages np;
+  __shared__ float* inbox_s[KVC_TP_MAX_WORLD];
+  for (int p = threadIdx.x; p < a.world; p += blockDim.x) inbox_s[p] = a.inbox[p];
+  const int l = blockIdx.y;
+  const int page0 = blockIdx.x * kNormPages;
+  norm_stage(np, st, page0, l, a.heads, a.total_pages, a.R, a.tokens, a.page_off, a.mean, a.den);
+  int64_t tok;
+  float4 z;
+  if (norm_quad(np, st, a.raw, l, a.heads, a.total_pages, page0, tok, z) > 0) {
+    const int64_t q = tok >> 2;
+    const int o = (int)(q / a.per);
+    float* dst = inbox_s[o] + (((int64_t)a.rank * a.L + l) * a.per + (q - (int64_t)o * a.per)) * 4;
+    *reinterpret_cast<float4*>(dst) = z;  // a peer store unless this rank owns the quad
+  }
+  __threadfence_system();  // this thread's stores before the completion count
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int32_t* counter = a.flags[a.rank] + tp_push_counter(a.world);
+    if (atomicAdd(counter, 1) == (int)(gridDim.x * gridDim.y) - 1) {
+      atomicExch(counter, 0);
+      __threadfence_system();
+      for (int p = 0; p < a.world; ++p) st_release_sys(a.flags[p] + a.rank, a.epoch);
+    }
+  }
+}
+
+// ---- exchange: reduce the owned quads from the local inbox, push the scores ----
+
+// W: the world size when it is compiled in (1, 2, 4, 8), else 0 (runtime).
 template <int W>
 __global__ void __launch_bounds__(kTpThreads) tp_reduce_push_kernel(const __grid_constant__ TpArgs a) {
   extern __shared__ float4 tp_sm[];  // [L][Q] per-layer maxima, then [Q] finished quads
   __shared__ int ok;
-  __shared__ const float* rows_s[KVC_TP_MAX_WORLD];
   __shared__ float* agg_s[KVC_TP_MAX_WORLD];
   const int world = W ? W : a.world;
-  for (int p = threadIdx.x; p < world; p += blockDim.x) {
-    rows_s[p] = a.rows[p];
-    agg_s[p] = a.agg[p];
-  }
+  for (int p = threadIdx.x; p < world; p += blockDim.x) agg_s[p] = a.agg[p];
   int32_t* mine = a.flags[a.rank];
   unsigned long long* stamps = reinterpret_cast<unsigned long long*>(mine + tp_stamp_word(world));
   if (threadIdx.x == 0) {
-    if (atomicExch(mine + 2 * world + 1, a.epoch) != a.epoch) {  // the first CTA of this step announces
+    if (atomicExch(mine + tp_started(world), a.epoch) != a.epoch) {  // the first CTA of this step
       stamps[1] = ~0ull;
       stamps[0] = tp_now_ns();
-      __threadfence_system();  // this rank's rows (previous kernel) and the stamps before "rows ready"
-      for (int p = 0; p < world; ++p) st_release_sys(a.flags[p] + a.rank, a.epoch);
     }
-    ok = wait_epochs(mine, world, a.epoch);
+    ok = wait_epochs(mine, world, a.epoch);  // every rank's rows delivered to this inbox
     if (ok) atomicMin(stamps + 1, (unsigned long long)tp_now_ns());
     else raise_flag(a.error_flag, KVC_DEV_TIMEOUT);
   }
@@ -131,21 +182,22 @@ __global__ void __launch_bounds__(kTpThreads) tp_reduce_push_kernel(const __grid
   float4* part = tp_sm;                   // [L][Q]
   float4* done = tp_sm + (int64_t)a.L * Q;  // [Q]
   if (ok) {
+    const float4* inbox = reinterpret_cast<const float4*>(a.inbox[a.rank]);
     const int64_t quads = a.tok_total >> 2;
-    const int64_t per = (quads + world - 1) / world;
-    const int64_t lo = (int64_t)a.rank * per;
-    const int64_t hi = min64(lo + per, quads);
+    const int64_t lo = (int64_t)a.rank * a.per;
+    const int64_t hi = min64(lo + a.per, quads);
+    const int64_t src_stride = (int64_t)a.L * a.per;  // float4s between two sources' blocks
     const int qi = threadIdx.x / LT, lt = threadIdx.x % LT;
     for (int64_t g0 = lo + (int64_t)blockIdx.x * Q; g0 < hi; g0 += (int64_t)gridDim.x * Q) {
       const int64_t q = g0 + qi;
-      if (qi < Q && q < hi && quad_valid(a, q << 2) > 0) {
+      if (qi < Q && q < hi && quad_valid(a.page_off, a.tokens, a.R, q << 2) > 0) {
         for (int l = lt; l < a.L; l += LT) {
-          const int64_t i = (int64_t)l * a.tok_total + (q << 2);
+          const float4* src = inbox + (int64_t)l * a.per + (q - lo);
           float4 m = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
           if constexpr (W > 0) {
             float4 x[W];
 #pragma unroll
-            for (int p = 0; p < W; ++p) x[p] = *reinterpret_cast<const float4*>(rows_s[p] + i);
+            for (int p = 0; p < W; ++p) x[p] = src[p * src_stride];
 #pragma unroll
             for (int p = 0; p < W; ++p) m = nan_max4(m, x[p]);
           } else {
@@ -153,7 +205,7 @@ __global__ void __launch_bounds__(kTpThreads) tp_reduce_push_kernel(const __grid
               float4 x[8];
 #pragma unroll
               for (int k = 0; k < 8; ++k)
-                if (p0 + k < world) x[k] = *reinterpret_cast<const float4*>(rows_s[p0 + k] + i);
+                if (p0 + k < world) x[k] = src[(p0 + k) * src_stride];
 #pragma unroll
               for (int k = 0; k < 8; ++k)
                 if (p0 + k < world) m = nan_max4(m, x[k]);
@@ -165,7 +217,7 @@ __global__ void __launch_bounds__(kTpThreads) tp_reduce_push_kernel(const __grid
       __syncthreads();
       if (threadIdx.x < Q && g0 + threadIdx.x < hi) {
         const int64_t tok = (g0 + threadIdx.x) << 2;
-        const int nv = quad_valid(a, tok);
+        const int nv = quad_valid(a.page_off, a.tokens, a.R, tok);
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);  // page padding, as kvc_aggregate_rows
         if (nv > 0) {
           float4 acc = part[threadIdx.x];
@@ -178,7 +230,7 @@ __global__ void __launch_bounds__(kTpThreads) tp_reduce_push_kernel(const __grid
             const float d = (float)a.L;
             acc = make_float4(__fdiv_rn(acc.x, d), __fdiv_rn(acc.y, d), __fdiv_rn(acc.z, d), __fdiv_rn(acc.w, d));
           }
-          v = make_float4(nv > 0 ? finalize_score(acc.x) : 0.f, nv > 1 ? finalize_score(acc.y) : 0.f,
+          v = make_float4(finalize_score(acc.x), nv > 1 ? finalize_score(acc.y) : 0.f,
                           nv > 2 ? finalize_score(acc.z) : 0.f, nv > 3 ? finalize_score(acc.w) : 0.f);
         }
         done[threadIdx.x] = v;
@@ -195,7 +247,7 @@ __global__ void __launch_bounds__(kTpThreads) tp_reduce_push_kernel(const __grid
   __threadfence_system();  // this thread's peer stores before the completion count
   __syncthreads();
   if (threadIdx.x == 0) {
-    int32_t* counter = mine + 2 * world;
+    int32_t* counter = mine + tp_exch_counter(world);
     if (atomicAdd(counter, 1) == (int)gridDim.x - 1) {
       atomicExch(counter, 0);
       stamps[2] = tp_now_ns();
@@ -222,10 +274,8 @@ template <int W>
 int launch_tp(const TpArgs& a, cudaStream_t st) {
   const int LT = std::min(a.L, 64), Q = kTpThreads / LT;
   const size_t smem = ((size_t)a.L * Q + Q) * sizeof(float4);
-  const int64_t quads = a.tok_total / 4;
-  const int64_t groups = ((quads + a.world - 1) / a.world + Q - 1) / Q;
-  // one wave at most: every CTA is resident, so the first CTA's signal and
-  // every CTA's wait run together
+  const int64_t groups = (a.per + Q - 1) / Q;
+  // one wave at most: every CTA is resident, so every CTA's wait runs together
   const int64_t cap = (int64_t)sm_count() * tp_blocks_per_sm<W>(smem);
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(groups, cap));
   tp_reduce_push_kernel<W><<<grid, kTpThreads, smem, st>>>(a);
@@ -252,23 +302,63 @@ extern "C" int kvc_tp_exchange_flag_words(int world) { return world > 0 ? tp_sta
 
 extern "C" int kvc_tp_exchange_stamp_word(int world) { return world > 0 ? tp_stamp_word(world) : 0; }
 
-extern "C" int kvc_tp_exchange_max(const float* const* peer_rows, float* const* peer_agg, int32_t* const* peer_flags,
+extern "C" int64_t kvc_tp_exchange_inbox_floats(int world, int num_layers, int total_pages) {
+  if (world < 1 || num_layers < 1 || total_pages < 0) return 0;
+  return (int64_t)world * num_layers * tp_quads_per_rank((int64_t)total_pages * kBlock, world) * 4;
+}
+
+extern "C" int kvc_tp_push_rows(const float* raw, int num_layers, int heads, int total_pages, const float* mean,
+                                const float* denom, const int32_t* tokens, const int32_t* page_off, int num_requests,
+                                float* const* peer_inbox, int32_t* const* peer_flags, int world, int rank,
+                                int32_t epoch, void* stream) {
+  KVC_CHECK_ARG(raw && mean && denom && tokens && page_off && peer_inbox && peer_flags, KVC_ENULL);
+  KVC_CHECK_ARG(world >= 1 && world <= KVC_TP_MAX_WORLD && rank >= 0 && rank < world, KVC_EINVAL);
+  KVC_CHECK_ARG(num_layers > 0 && num_layers <= 65535 && heads > 0 && total_pages >= 0 && num_requests >= 0 &&
+                    epoch > 0,
+                KVC_EINVAL);
+  KVC_CHECK_ARG(aligned(raw, 16), KVC_EALIGN);
+  const size_t smem = (size_t)3 * kNormPages * heads * sizeof(float);
+  KVC_CHECK_ARG(smem <= 48 * 1024, KVC_EUNSUPPORTED);
+  PushArgs a{};
+  a.raw = raw;
+  a.mean = mean;
+  a.den = denom;
+  a.tokens = tokens;
+  a.page_off = page_off;
+  a.inbox = peer_inbox;
+  a.flags = peer_flags;
+  a.per = tp_quads_per_rank((int64_t)total_pages * kBlock, world);
+  a.L = num_layers;
+  a.heads = heads;
+  a.total_pages = total_pages;
+  a.R = num_requests;
+  a.world = world;
+  a.rank = rank;
+  a.epoch = epoch;
+  // every rank launches every step, even with no tokens, so the epochs of all ranks advance together
+  const dim3 grid((unsigned)std::max(1, (total_pages + kNormPages - 1) / kNormPages), (unsigned)num_layers);
+  tp_push_rows_kernel<<<grid, 256, smem, (cudaStream_t)stream>>>(a);
+  return launch_status();
+}
+
+extern "C" int kvc_tp_exchange_max(float* const* peer_inbox, float* const* peer_agg, int32_t* const* peer_flags,
                                    int world, int rank, int num_layers, int total_pages, const int32_t* tokens,
                                    const int32_t* page_off, int num_requests, int layer_aggregation, int32_t epoch,
                                    int32_t* error_flag, void* stream) {
-  KVC_CHECK_ARG(peer_rows && peer_agg && peer_flags && tokens && page_off, KVC_ENULL);
+  KVC_CHECK_ARG(peer_inbox && peer_agg && peer_flags && tokens && page_off, KVC_ENULL);
   KVC_CHECK_ARG(world >= 1 && world <= KVC_TP_MAX_WORLD && rank >= 0 && rank < world, KVC_EINVAL);
   KVC_CHECK_ARG(num_layers > 0 && total_pages >= 0 && num_requests >= 0 && epoch > 0, KVC_EINVAL);
   KVC_CHECK_ARG(num_layers <= kTpMaxLayers, KVC_EUNSUPPORTED);
   KVC_CHECK_ARG(layer_aggregation == KVC_AGG_MEAN || layer_aggregation == KVC_AGG_MAX, KVC_EINVAL);
   TpArgs a{};
-  a.rows = peer_rows;
+  a.inbox = peer_inbox;
   a.agg = peer_agg;
   a.flags = peer_flags;
   a.tokens = tokens;
   a.page_off = page_off;
   a.error_flag = error_flag;
   a.tok_total = (int64_t)total_pages * kBlock;
+  a.per = tp_quads_per_rank(a.tok_total, world);
   a.world = world;
   a.rank = rank;
   a.L = num_layers;

@@ -69,6 +69,8 @@ _SIGNATURES = {
         c_int, [_P, c_int, c_int64, c_int64, c_int, c_int, c_int, _P, _P, _P, _P, _P]),
     "kvc_tp_exchange_flag_words": (c_int, [c_int]),
     "kvc_tp_exchange_stamp_word": (c_int, [c_int]),
+    "kvc_tp_exchange_inbox_floats": (c_int64, [c_int, c_int, c_int]),
+    "kvc_tp_push_rows": (c_int, [_P, c_int, c_int, c_int, _P, _P, _P, _P, c_int, _P, _P, c_int, c_int, c_int32, _P]),
     "kvc_tp_exchange_max": (
         c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, _P, _P, c_int, c_int, c_int32, _P, _P]),
     "kvc_ipc_export": (c_int, [c_int, _P, _P, _P]),
@@ -109,7 +111,7 @@ class TriAttentionStep(ctypes.Structure):
         ("agg", _P), ("keep", _P), ("staged_rows", _P), ("staged_row_stride", c_int32), ("staged_offsets", _P),
         ("error_flag", _P), ("cache_blocks_per_page", c_int32),
         ("error_host", _P), ("error_event", _P),
-        ("peer_rows", _P), ("peer_agg", _P), ("peer_flags", _P), ("world", c_int32), ("rank", c_int32),
+        ("peer_inbox", _P), ("peer_agg", _P), ("peer_flags", _P), ("world", c_int32), ("rank", c_int32),
         ("epoch", c_int32),
     ]
 

@@ -727,13 +727,12 @@ class TriAttentionMethod(KVCompressionMethod):
         head = N.STAGE_TABLES | N.STAGE_SCORE
         ex = self._peer
         if ex is not None:
-            # rows go straight into the peer-mapped exchange buffer; the exchange
-            # kernel replaces the all-reduce and the layer reduction, inside the
-            # same native call as the other stages
+            # normalisation pushes each rank's rows into the owners' inboxes and
+            # the exchange kernel replaces the all-reduce and the layer reduction,
+            # inside the same native call as the other stages
             ex.ensure(L, tok)
-            st.rows = ex.rows_ptr
             st.agg = ex.agg_ptr
-            st.peer_rows, st.peer_agg, st.peer_flags = ex.tables()
+            st.peer_inbox, st.peer_agg, st.peer_flags = ex.tables()
             st.world, st.rank = ex.world, ex.rank
             st.epoch = ex.next_epoch()
             stages = head | N.STAGE_EXCHANGE | (tail & ~N.STAGE_AGGREGATE)

@@ -1,14 +1,15 @@
-"""Tensor-parallel score sync over NVLink peer memory (CUDA IPC + one kernel).
+"""Tensor-parallel score sync over NVLink peer memory (CUDA IPC + two kernels).
 
 The reference synchronises the per-layer head-max rows of a TP group with one
 MAX all-reduce and then reduces the layers on every rank
-(src/vllm_ascend_kvcompress/methods/triattention/method.py:447-467).  Here each
-rank's rows live in an exchange buffer that every other rank of the group has
-mapped through CUDA IPC; ``kvc_tp_exchange_max`` has each rank reduce its
-1/world share of the tokens over all ranks' rows, reduce the layers, and store
-the finished scores into every rank's agg buffer.  The scores are bit-identical
-to the all-reduce path (MAX commutes with the head sharding; the layer
-reduction is the same sequential code).
+(src/vllm_ascend_kvcompress/methods/triattention/method.py:447-467).  Here the
+step's tokens are split into one range per rank; each rank's normalisation
+stores its rows of every range straight into the owning rank's inbox (mapped
+through CUDA IPC), and ``kvc_tp_exchange_max`` has each rank reduce its range
+over all ranks' rows from its own inbox, reduce the layers, and store the
+finished scores into every rank's agg buffer.  The scores are bit-identical to
+the all-reduce path (MAX commutes with the head sharding; the layer reduction
+is the same sequential code).
 
 ``PeerScoreExchange`` owns the buffers of one rank.  Growing them is a
 collective: every rank of the group must call ``ensure`` with the same
@@ -30,12 +31,18 @@ _ALIGN = 256
 
 
 def exchange_layout(world: int, layers: int, cap_tokens: int, flag_words: int) -> tuple[int, int, int, int]:
-    """(flags, agg, rows) byte offsets and total bytes of one rank's exchange buffer."""
+    """(flags, agg, inbox) byte offsets and total bytes of one rank's exchange buffer.
+
+    The inbox holds [world source ranks][layers][quads per rank][4] fp32, for
+    steps of up to ``cap_tokens`` page-padded tokens (quads of 4 tokens, split
+    evenly over the ranks, as kvc_tp_exchange_inbox_floats sizes it).
+    """
     up = lambda n: -(-n // _ALIGN) * _ALIGN
     flags = 0
     agg = up(flag_words * 4)
-    rows = agg + up(cap_tokens * 4)
-    return flags, agg, rows, rows + up(layers * cap_tokens * 4)
+    inbox = agg + up(cap_tokens * 4)
+    per = -(-(-(-cap_tokens // 4)) // world)
+    return flags, agg, inbox, inbox + up(world * layers * per * 16)
 
 
 def ipc_capable_allocator() -> bool:
@@ -82,7 +89,7 @@ class PeerScoreExchange:
         self.buf: torch.Tensor | None = None
         self.opened: list[int] = []
         self.table: torch.Tensor | None = None
-        self.rows_ptr = self.agg_ptr = 0
+        self.inbox_ptr = self.agg_ptr = 0
         self.epoch = 0
 
     def ensure(self, layers: int, tok_total: int) -> None:
@@ -104,7 +111,7 @@ class PeerScoreExchange:
         self.close()
         dist.barrier(group=self.group)
         self.buf = None
-        flags_off, agg_off, rows_off, total = exchange_layout(self.world, layers, cap, self.flag_words)
+        flags_off, agg_off, inbox_off, total = exchange_layout(self.world, layers, cap, self.flag_words)
         buf = torch.zeros(total, dtype=torch.uint8, device=self.device)
         handle = (ctypes.c_char * N.IPC_HANDLE_BYTES)()
         off = ctypes.c_int64()
@@ -122,12 +129,12 @@ class PeerScoreExchange:
             N.check(lib.kvc_ipc_open(dev, hb, ctypes.byref(base)), "kvc_ipc_open")
             self.opened.append(base.value)
             bases.append(base.value + o)
-        self.table = torch.tensor([b + rows_off for b in bases] + [b + agg_off for b in bases]
+        self.table = torch.tensor([b + inbox_off for b in bases] + [b + agg_off for b in bases]
                                   + [b + flags_off for b in bases], dtype=torch.int64, device=self.device)
         self.buf = buf
         self.layers = layers
         self.cap_tokens = cap
-        self.rows_ptr = buf.data_ptr() + rows_off
+        self.inbox_ptr = buf.data_ptr() + inbox_off
         self.agg_ptr = buf.data_ptr() + agg_off
         self._agg_off = agg_off
         torch.cuda.synchronize(self.device)
@@ -143,7 +150,7 @@ class PeerScoreExchange:
         return self.buf[4 * w: 4 * w + 32].view(torch.int64)
 
     def tables(self) -> tuple[int, int, int]:
-        """Device addresses of the rows, agg and flags tables (``world`` addresses each)."""
+        """Device addresses of the inbox, agg and flags tables (``world`` addresses each)."""
         t = self.table.data_ptr()
         return t, t + 8 * self.world, t + 16 * self.world
 
@@ -151,14 +158,6 @@ class PeerScoreExchange:
         """The epoch of the next exchange (every rank advances it once per step)."""
         self.epoch += 1
         return self.epoch
-
-    def exchange(self, layers: int, total_pages: int, tokens: int, page_off: int, num_requests: int,
-                 layer_aggregation: int, error_flag: int, stream: int) -> None:
-        """Queue this rank's share of a sync on ``stream`` as a call of its own (all ranks call it)."""
-        rows, agg, flags = self.tables()
-        N.check(N.lib().kvc_tp_exchange_max(rows, agg, flags, self.world, self.rank, layers, total_pages, tokens,
-                                            page_off, num_requests, layer_aggregation, self.next_epoch(),
-                                            error_flag, stream), "kvc_tp_exchange_max")
 
     def close(self) -> None:
         """Unmap the other ranks' buffers (callers synchronise first); this rank's buffer stays."""
