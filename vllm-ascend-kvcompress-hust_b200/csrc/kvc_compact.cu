@@ -470,15 +470,17 @@ extern "C" int kvc_compact(const void* const* k_layers, const void* const* v_lay
     a.R = R;
     a.budget = budget;
     const int64_t rows = (int64_t)a.N * 2 * R * budget;
-    // enough warps to fill the GPU: shrink the per-warp tile when rows are few
-    const int64_t full = (int64_t)sm_count() * (2048 / 32);
-    a.tile_rows = (int)std::max<int64_t>(1, std::min<int64_t>(32, rows / full));
-    const int64_t nvec = row_bytes / vec;
-    a.nvec_shift = (nvec & (nvec - 1)) == 0 ? __builtin_ctzll((unsigned long long)nvec) : -1;
-    const int64_t tiles = (rows + a.tile_rows - 1) / a.tile_rows;
     // bulk copies pay off for rows of 1 KB and more (per-copy overhead dominates below)
     const bool bulk = vec >= 16 && row_bytes % 16 == 0 && row_bytes >= 1024 && row_bytes <= kBulkWarpBytes / 2 &&
                       bulk_ready();
+    // enough warps to fill the GPU: shrink the per-warp tile when rows are few,
+    // but give every warp of the chosen kernel all its rows in one tile (a warp
+    // resolves and copies a tile's rows together; tiles run one after another)
+    const int64_t warps = (int64_t)sm_count() * (bulk ? kBulkWarps : 2048 / 32);
+    a.tile_rows = (int)std::max<int64_t>(1, std::min<int64_t>(32, bulk ? (rows + warps - 1) / warps : rows / warps));
+    const int64_t nvec = row_bytes / vec;
+    a.nvec_shift = (nvec & (nvec - 1)) == 0 ? __builtin_ctzll((unsigned long long)nvec) : -1;
+    const int64_t tiles = (rows + a.tile_rows - 1) / a.tile_rows;
     if (bulk) {
       const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(sm_count(), (tiles + kBulkWarps - 1) / kBulkWarps));
       compact_bulk_kernel<<<grid, kBulkWarps * 32, kBulkSmem, st>>>(a);
