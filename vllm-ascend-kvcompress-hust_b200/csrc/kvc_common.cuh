@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "kvc.h"
 
 namespace kvc {
@@ -110,6 +112,35 @@ __device__ __forceinline__ int request_of_page(const int32_t* __restrict__ page_
 
 __device__ __forceinline__ void raise_flag(int32_t* flag, int bit) {
   if (flag) atomicOr(flag, bit);
+}
+
+// ---- programmatic dependent launch ---------------------------------------
+//
+// The kernels of a compression step run back to back on one stream.  Each
+// starts with pdl_wait() -- before touching any global memory -- which returns
+// once the preceding kernel on the stream has completed and its writes are
+// visible (and at once when the kernel was launched without the attribute),
+// then calls pdl_trigger(), which lets the next kernel be launched while this
+// one still runs.  launch_dep() launches with programmatic stream
+// serialization, so the next kernel's CTAs are resident and waiting when this
+// one ends instead of being launched after it.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... Params, typename... Args>
+inline void launch_dep(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 }  // namespace kvc

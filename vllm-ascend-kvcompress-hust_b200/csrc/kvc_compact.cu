@@ -151,6 +151,8 @@ __device__ __forceinline__ void fetch_end(const CompactArgs& a, const RowFetch& 
 
 template <int VEC, bool SMALL>
 __global__ void __launch_bounds__(kCopyThreads, SMALL ? 2 : 4) compact_kernel(const __grid_constant__ CompactArgs a) {
+  pdl_wait();  // the preceding kernel of the step has finished (see kvc_common.cuh)
+  pdl_trigger();
   using T = typename Vec<VEC>::T;
   const int lane = threadIdx.x & 31;
   const int64_t rows = (int64_t)a.N * 2 * a.R * a.budget;
@@ -262,6 +264,8 @@ constexpr int kBulkWarpBytes = 24 * 1024;
 constexpr int kBulkSmem = kBulkWarps * kBulkWarpBytes;
 
 __global__ void __launch_bounds__(kBulkWarps * 32, 1) compact_bulk_kernel(const __grid_constant__ CompactArgs a) {
+  pdl_wait();  // the preceding kernel of the step has finished (see kvc_common.cuh)
+  pdl_trigger();
   extern __shared__ __align__(128) uint8_t bulk_sm[];
   __shared__ __align__(8) uint64_t bars[kBulkWarps][2];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -322,6 +326,8 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1) compact_bulk_kernel(const 
 __global__ void stage_commit_kernel(const int64_t* __restrict__ dst_blocks, const int64_t* __restrict__ dst_block_off,
                                     int R, int bpp, int64_t* staged_rows, int stride, int64_t* staged_offsets,
                                     const int64_t* __restrict__ semantic, int budget) {
+  pdl_wait();  // the preceding kernel of the step has finished (see kvc_common.cuh)
+  pdl_trigger();
   const int r = blockIdx.x;
   const int64_t b0 = dst_block_off[r], b1 = dst_block_off[r + 1];
   if (staged_rows)
@@ -422,7 +428,8 @@ bool bulk_ready() {
 
 template <int VEC, bool SMALL>
 void launch_compact(const CompactArgs& a, int64_t tiles, cudaStream_t st) {
-  compact_kernel<VEC, SMALL><<<copy_grid(tiles, compact_blocks_per_sm<VEC, SMALL>()), kCopyThreads, 0, st>>>(a);
+  launch_dep(compact_kernel<VEC, SMALL>, dim3(copy_grid(tiles, compact_blocks_per_sm<VEC, SMALL>())),
+             dim3(kCopyThreads), 0, st, a);
 }
 
 }  // namespace kvc
@@ -483,7 +490,7 @@ extern "C" int kvc_compact(const void* const* k_layers, const void* const* v_lay
     const int64_t tiles = (rows + a.tile_rows - 1) / a.tile_rows;
     if (bulk) {
       const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(sm_count(), (tiles + kBulkWarps - 1) / kBulkWarps));
-      compact_bulk_kernel<<<grid, kBulkWarps * 32, kBulkSmem, st>>>(a);
+      launch_dep(compact_bulk_kernel, dim3(grid), dim3(kBulkWarps * 32), kBulkSmem, st, a);
     } else if (row_bytes < 2048) {
       switch (vec) {
         case 32: launch_compact<32, true>(a, tiles, st); break;
@@ -505,8 +512,8 @@ extern "C" int kvc_compact(const void* const* k_layers, const void* const* v_lay
     if (rc != KVC_OK) return rc;
   }
   if (staged_rows || (staged_offsets && semantic)) {
-    stage_commit_kernel<<<R, 128, 0, st>>>(dst_blocks, dst_block_off, R, 1, staged_rows, staged_row_stride,
-                                           staged_offsets, semantic, budget);
+    launch_dep(stage_commit_kernel, dim3(R), dim3(128), 0, st, dst_blocks, dst_block_off, R, 1, staged_rows,
+               staged_row_stride, staged_offsets, semantic, budget);
     return launch_status();
   }
   return KVC_OK;
@@ -520,10 +527,8 @@ extern "C" int kvc_stage_commit(const int64_t* dst_blocks, const int64_t* dst_bl
   KVC_CHECK_ARG(num_requests >= 0 && blocks_per_page >= 1 && budget > 0, KVC_EINVAL);
   KVC_CHECK_ARG(staged_rows == nullptr || staged_row_stride > 0, KVC_EINVAL);
   if (num_requests == 0 || (!staged_rows && !staged_offsets)) return KVC_OK;
-  stage_commit_kernel<<<num_requests, 128, 0, (cudaStream_t)stream>>>(dst_blocks, dst_block_off, num_requests,
-                                                                      blocks_per_page, staged_rows,
-                                                                      staged_row_stride, staged_offsets, semantic,
-                                                                      budget);
+  launch_dep(stage_commit_kernel, dim3(num_requests), dim3(128), 0, (cudaStream_t)stream, dst_blocks, dst_block_off,
+             num_requests, blocks_per_page, staged_rows, staged_row_stride, staged_offsets, semantic, budget);
   return launch_status();
 }
 

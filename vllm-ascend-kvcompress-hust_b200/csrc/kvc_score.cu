@@ -40,6 +40,8 @@ struct PrepArgs {
 };
 
 __global__ void __launch_bounds__(256) prepare_coef_kernel(PrepArgs a) {
+  pdl_wait();  // the preceding kernel of the step has finished (see kvc_common.cuh)
+  pdl_trigger();
   extern __shared__ float sm[];
   float* cmean = sm;              // [F]
   float* smean = sm + a.F;        // [F]
@@ -248,6 +250,8 @@ __device__ __forceinline__ bool unit_page(const ScoreArgs& a, int p, int& r, int
 
 template <int G, class E>
 __global__ void __launch_bounds__(kScoreWarps * 32, 2) score_mean_kernel(const __grid_constant__ ScoreArgs a) {
+  pdl_wait();  // the preceding kernel of the step has finished (see kvc_common.cuh)
+  pdl_trigger();
   extern __shared__ float4 smem4[];
   constexpr int CG = coef_group_stride(G);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -313,6 +317,8 @@ __global__ void __launch_bounds__(kScoreWarps * 32, 2) score_mean_kernel(const _
 
 template <int G, class E>
 __global__ void __launch_bounds__(kScoreWarps * 32) score_max_kernel(const __grid_constant__ ScoreArgs a) {
+  pdl_wait();  // the preceding kernel of the step has finished (see kvc_common.cuh)
+  pdl_trigger();
   constexpr int CG = coef_group_stride(G);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t units = (int64_t)a.L * a.total_pages * a.kvh;
@@ -396,6 +402,8 @@ __global__ void __launch_bounds__(1024) head_stats_kernel(const float* __restric
                                                           const int32_t* __restrict__ tokens,
                                                           const int32_t* __restrict__ page_off,
                                                           float* mean_out, float* var_out, float* den_out) {
+  pdl_wait();  // the preceding kernel of the step has finished (see kvc_common.cuh)
+  pdl_trigger();
   extern __shared__ double red[];  // [blockDim]
   __shared__ double mean_s[1024];
   const int l = blockIdx.x, r = blockIdx.y;
@@ -473,6 +481,8 @@ __global__ void __launch_bounds__(256) normalize_kernel(const float* __restrict_
                                                         const int32_t* __restrict__ tokens,
                                                         const int32_t* __restrict__ page_off, int R,
                                                         float* rows) {
+  pdl_wait();  // the preceding kernel of the step has finished (see kvc_common.cuh)
+  pdl_trigger();
   extern __shared__ float st[];  // [3][kNormPages][heads]
   __shared__ NormPages np;
   const int l = blockIdx.y;
@@ -490,6 +500,8 @@ __global__ void __launch_bounds__(256) aggregate_rows_kernel(const float* __rest
                                                              const int32_t* __restrict__ tokens,
                                                              const int32_t* __restrict__ page_off, int R,
                                                              int layer_agg, float* agg) {
+  pdl_wait();  // the preceding kernel of the step has finished (see kvc_common.cuh)
+  pdl_trigger();
   const int64_t first = (int64_t)blockIdx.x * blockDim.x;  // 256 tokens: two pages
   const int r_lo = request_of_page(page_off, R, (int)(first >> 7));
   const int r_hi = request_of_page(page_off, R, (int)((min64(first + blockDim.x, tok_total) - 1) >> 7));
@@ -533,9 +545,9 @@ int launch_score(const ScoreArgs& a, int aggregation, cudaStream_t st) {
         return KVC_ECUDA;
       configured[dev] = smem;
     }
-    score_mean_kernel<G, E><<<grid, kScoreWarps * 32, smem, st>>>(a);
+    launch_dep(score_mean_kernel<G, E>, grid, dim3(kScoreWarps * 32), smem, st, a);
   } else {
-    score_max_kernel<G, E><<<grid, kScoreWarps * 32, 0, st>>>(a);
+    launch_dep(score_max_kernel<G, E>, grid, dim3(kScoreWarps * 32), 0, st, a);
   }
   (void)CG;
   return launch_status();
@@ -583,7 +595,7 @@ extern "C" int kvc_prepare_score_coefficients(const float* omega, const float* o
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(prepare_coef_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return KVC_ECUDA;
-  prepare_coef_kernel<<<dim3(L, R), 256, smem, (cudaStream_t)stream>>>(a);
+  launch_dep(prepare_coef_kernel, dim3(L, R), dim3(256), smem, (cudaStream_t)stream, a);
   return launch_status();
 }
 
@@ -656,8 +668,8 @@ extern "C" int kvc_head_stats(const float* partial, int L, int R, int total_page
   // the largest whole number of threads per head that fits 1024 threads
   const int threads = (1024 / heads) * heads;
   const int block = std::min(1024, ((threads + 31) / 32) * 32);
-  head_stats_kernel<<<dim3(L, R), block, block * sizeof(double), (cudaStream_t)stream>>>(
-      partial, L, R, total_pages, parts_per_page, heads, tokens, page_off, mean_out, var_out, denom_out);
+  launch_dep(head_stats_kernel, dim3(L, R), dim3(block), block * sizeof(double), (cudaStream_t)stream, partial, L, R,
+             total_pages, parts_per_page, heads, tokens, page_off, mean_out, var_out, denom_out);
   return launch_status();
 }
 
@@ -674,7 +686,8 @@ extern "C" int kvc_normalize_aggregate(const float* raw, int L, int heads, int t
   const size_t smem = (size_t)3 * kNormPages * heads * sizeof(float);
   if (smem > 48 * 1024) return KVC_EUNSUPPORTED;
   cudaStream_t st = (cudaStream_t)stream;
-  normalize_kernel<<<grid, 256, smem, st>>>(raw, L, heads, total_pages, mean, denom, tokens, page_off, R, rows_out);
+  launch_dep(normalize_kernel, grid, dim3(256), smem, st, raw, L, heads, total_pages, mean, denom, tokens, page_off, R,
+             rows_out);
   const int rc = launch_status();
   if (rc != KVC_OK || agg_out == nullptr) return rc;
   return kvc_aggregate_rows(rows_out, L, total_pages, tokens, page_off, R, layer_aggregation, agg_out, stream);
@@ -688,7 +701,7 @@ extern "C" int kvc_aggregate_rows(const float* rows, int L, int total_pages, con
   KVC_CHECK_ARG(layer_aggregation == KVC_AGG_MEAN || layer_aggregation == KVC_AGG_MAX, KVC_EINVAL);
   if (R == 0 || total_pages == 0) return KVC_OK;
   const int64_t tok_total = (int64_t)total_pages * kBlock;
-  aggregate_rows_kernel<<<(unsigned)((tok_total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-      rows, L, tok_total, tokens, page_off, R, layer_aggregation, agg_out);
+  launch_dep(aggregate_rows_kernel, dim3((unsigned)((tok_total + 255) / 256)), dim3(256), 0, (cudaStream_t)stream, rows,
+             L, tok_total, tokens, page_off, R, layer_aggregation, agg_out);
   return launch_status();
 }

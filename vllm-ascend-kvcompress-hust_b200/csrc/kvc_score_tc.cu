@@ -70,6 +70,8 @@ __device__ __forceinline__ float from_half_bits(uint16_t v, int fp16) {
 }
 
 __global__ void __launch_bounds__(256) prepare_frag_kernel(const __grid_constant__ FragArgs a) {
+  pdl_wait();  // the preceding kernel of the step has finished (see kvc_common.cuh)
+  pdl_trigger();
   extern __shared__ float sm[];
   float* cm = sm;                      // [F] mean cos
   float* sn = sm + a.F;                // [F] mean sin
@@ -284,6 +286,8 @@ struct UnitMeta {
 // registers, which leaves room for three CTAs per SM.
 template <int F, int P, class E>
 __global__ void __launch_bounds__(kTcThreads, TcGeom<F, P>::kMinBlocks) score_tc_kernel(const __grid_constant__ TcArgs a) {
+  pdl_wait();  // the preceding kernel of the step has finished (see kvc_common.cuh)
+  pdl_trigger();
   using Gm = TcGeom<F, P>;
   constexpr int KF = F / 16;
   constexpr int KP = P / 16;
@@ -513,7 +517,7 @@ int launch_tc(const TcArgs& a, cudaStream_t st) {
   }
   const int64_t cap = (int64_t)sm_count() * Gm::kMinBlocks;
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cap, a.units));
-  score_tc_kernel<F, P, E><<<grid, kTcThreads, Gm::kSmem, st>>>(a);
+  launch_dep(score_tc_kernel<F, P, E>, dim3(grid), dim3(kTcThreads), Gm::kSmem, st, a);
   return launch_status();
 }
 
@@ -595,7 +599,7 @@ extern "C" int kvc_prepare_score_fragments(const float* omega, const float* offs
              n_off, R, L, kvh, G, F, P, dtype == KVC_FP16 ? 1 : 0};
   const size_t smem = ((size_t)(2 + 2 * n_off) * F + (size_t)4 * G * F) * sizeof(float);
   KVC_CHECK_ARG(smem <= 48 * 1024, KVC_EUNSUPPORTED);
-  prepare_frag_kernel<<<dim3(L, R, kvh), 256, smem, (cudaStream_t)stream>>>(a);
+  launch_dep(prepare_frag_kernel, dim3(L, R, kvh), dim3(256), smem, (cudaStream_t)stream, a);
   return launch_status();
 }
 

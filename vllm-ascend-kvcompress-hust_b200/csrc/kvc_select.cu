@@ -62,6 +62,8 @@ struct SelectArgs {
 };
 
 __global__ void __launch_bounds__(kSelThreads) select_kernel(const __grid_constant__ SelectArgs a) {
+  pdl_wait();  // the preceding kernel of the step has finished (see kvc_common.cuh)
+  pdl_trigger();
   __shared__ uint32_t hist[256];
   __shared__ uint32_t warp_tot[kSelWarps];
   __shared__ uint32_t s_digit, s_above;
@@ -182,6 +184,6 @@ extern "C" int kvc_select_keep(const float* agg, const int32_t* tokens, const in
   if (R == 0) return KVC_OK;
   SelectArgs a{agg, tokens, page_off, keep_out, error_flag, R, budget, prefix, recent, segments, policy};
   const int S = policy == KVC_POLICY_GLOBAL ? 1 : segments;
-  select_kernel<<<dim3(S, R), kSelThreads, 0, (cudaStream_t)stream>>>(a);
+  launch_dep(select_kernel, dim3(S, R), dim3(kSelThreads), 0, (cudaStream_t)stream, a);
   return launch_status();
 }

@@ -17,6 +17,9 @@ __global__ void gather_tables_kernel(const int64_t* const* __restrict__ src_tabl
                                      const int64_t* __restrict__ src_off, int64_t* src_out,
                                      const int64_t* const* __restrict__ dst_tables,
                                      const int64_t* __restrict__ dst_off, int64_t* dst_out, int bpp) {
+  // first kernel of the step, launched in plain stream order; lets the next
+  // stage's CTAs onto the SMs early (they wait for this grid in pdl_wait)
+  kvc::pdl_trigger();
   const int r = blockIdx.x;
   const int64_t* const* tables = blockIdx.y ? dst_tables : src_tables;
   const int64_t* off = blockIdx.y ? dst_off : src_off;

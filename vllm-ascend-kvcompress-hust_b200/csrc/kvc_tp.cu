@@ -128,6 +128,8 @@ struct PushArgs {
 };
 
 __global__ void __launch_bounds__(256) tp_push_rows_kernel(const __grid_constant__ PushArgs a) {
+  pdl_wait();  // the preceding kernel of the step has finished (see kvc_common.cuh)
+  pdl_trigger();
   extern __shared__ float st[];  // [3][kNormPages][heads]
   __shared__ NormPages np;
   __shared__ float* inbox_s[KVC_TP_MAX_WORLD];
@@ -160,6 +162,8 @@ __global__ void __launch_bounds__(256) tp_push_rows_kernel(const __grid_constant
 // W: the world size when it is compiled in (1, 2, 4, 8), else 0 (runtime).
 template <int W>
 __global__ void __launch_bounds__(kTpThreads) tp_reduce_push_kernel(const __grid_constant__ TpArgs a) {
+  // launched in plain stream order and without early dependents: its CTAs spin on
+  // peer flags, so nothing else is let onto the SMs beside them
   extern __shared__ float4 tp_sm[];  // [L][Q] per-layer maxima, then [Q] finished quads
   __shared__ int ok;
   __shared__ float* agg_s[KVC_TP_MAX_WORLD];
@@ -337,7 +341,7 @@ extern "C" int kvc_tp_push_rows(const float* raw, int num_layers, int heads, int
   a.epoch = epoch;
   // every rank launches every step, even with no tokens, so the epochs of all ranks advance together
   const dim3 grid((unsigned)std::max(1, (total_pages + kNormPages - 1) / kNormPages), (unsigned)num_layers);
-  tp_push_rows_kernel<<<grid, 256, smem, (cudaStream_t)stream>>>(a);
+  launch_dep(tp_push_rows_kernel, grid, dim3(256), smem, (cudaStream_t)stream, a);
   return launch_status();
 }
 
