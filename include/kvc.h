@@ -143,6 +143,32 @@ int kvc_score_paged_keys_tc(const void* key_maps, int num_layers, int dtype, int
                             int32_t* error_flag, void* stream);
 
 /*
+ * The same scorer on the 5th-generation tensor cores (tcgen05): per
+ * (page, KV head) tile, M = 128 tokens x N = 16 x K = 16 tcgen05.mma steps
+ * with the fp32 accumulator in tensor memory; the rotary band's A operand
+ * (kr | ki | m_hi | m_lo) is formed by the CUDA cores into TMEM, the pass band
+ * is read from the TMA-staged tile through shared-memory descriptors.  Same
+ * arguments, outputs and partials as kvc_score_paged_keys_tc, but its W layout
+ * differs: frag must come from kvc_prepare_score_fragments_tc05 (same size,
+ * kvc_fragment_words).  Geometries: kvc_tc05_supported (query group <= 8,
+ * (rotary/2, head_dim - rotary) in {(64,0), (32,0), (32,192), (32,64),
+ * (64,128)}).  One CTA per SM holds all 512 TMEM columns.
+ */
+int kvc_tc05_supported(int group, int head_dim, int rotary_dim);
+int kvc_prepare_score_fragments_tc05(const float* omega, const float* offsets, int n_off,
+                                     const int64_t* round_start, int num_requests, int num_layers,
+                                     int kv_heads, int group, int num_freq, int pass_dim,
+                                     const float* q_real, const float* q_imag, const float* scale,
+                                     const float* extra, const float* q_pass, int dtype, uint32_t* frag_out,
+                                     void* stream);
+int kvc_score_paged_keys_tc05(const void* key_maps, int num_layers, int dtype, int64_t num_blocks,
+                              int kv_heads, int group, int head_dim, int rotary_dim,
+                              const int64_t* src_blocks, const int64_t* src_block_off,
+                              const int32_t* tokens, const int32_t* page_off, int num_requests,
+                              int total_pages, const uint32_t* frag, float* raw_out, float* partial_out,
+                              int32_t* error_flag, void* stream);
+
+/*
  * Per (scoring layer, request, query head) population mean/variance of the
  * raw scores, combined from the partial moments in fp64; denom = sqrt(max(var, 1e-6)).
  * parts_per_page: 1 (kvc_score_paged_keys) or kvc_tc_partials_per_page()
@@ -476,6 +502,7 @@ int kvc_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
  */
 #define KVC_SCORER_TENSOR 0     /* kvc_score_paged_keys_tc (needs key_maps) */
 #define KVC_SCORER_FMA 1        /* kvc_score_paged_keys (needs score_k) */
+#define KVC_SCORER_TCGEN05 2    /* kvc_score_paged_keys_tc05 (needs key_maps) */
 #define KVC_STAGE_SCORE 1
 #define KVC_STAGE_AGGREGATE 2
 #define KVC_STAGE_SELECT 4

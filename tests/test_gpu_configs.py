@@ -102,3 +102,13 @@ def test_config3_full_layer_against_fp64():
         g_mean, w_mean = got / n_tok, want / n_tok
         err = float((g_mean - w_mean).abs().max())
         assert err <= 1e-4 * max(float(w_mean.abs().max()), mean_abs), err
+
+
+@pytest.mark.parametrize("which", ["config1", "config2"])
+def test_tcgen05_scorer_at_config_shapes(which, tmp_path, monkeypatch):
+    """The TMEM-accumulator scorer (opt-in) meets the same bar at the benchmark shapes."""
+    monkeypatch.setenv("KVC_B200_SCORER", "tcgen05")
+    if which == "config1":
+        _run(_config1(8, [4736, 32768]), distinct=3, tmp_path=tmp_path)
+    else:
+        _run(_config2(), distinct=5, tmp_path=tmp_path, bpp=16)

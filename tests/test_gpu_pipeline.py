@@ -37,7 +37,9 @@ def _workload(name: str) -> W.Workload:
 
 
 @pytest.mark.parametrize("name,scorer", [("config0", "auto"), ("partial", "auto"), ("global_max", "auto"),
-                                         ("score_max", "auto"), ("config0", "fma"), ("partial", "fma")])
+                                         ("score_max", "auto"), ("config0", "fma"), ("partial", "fma"),
+                                         ("config0", "tcgen05"), ("partial", "tcgen05"),
+                                         ("global_max", "tcgen05")])
 def test_pipeline_matches_reference_golden(name, scorer, tmp_path, monkeypatch):
     monkeypatch.setenv("KVC_B200_SCORER", scorer)
     arrays, spec = golden()
@@ -47,6 +49,7 @@ def test_pipeline_matches_reference_golden(name, scorer, tmp_path, monkeypatch):
     m = bind(w, gpu, tmp_path)
     if name != "score_max" and scorer == "auto":
         assert m.use_tensor_scorer, "supported geometry must take the tensor-core scorer"
+    assert m.use_tcgen05 == (scorer == "tcgen05")
     reqs = W.b200_requests(w)
     idx = w.compressed()
     keep = m.select_many(reqs).cpu()
@@ -86,14 +89,15 @@ def test_tensor_and_cuda_core_scorers_agree(tmp_path, monkeypatch):
     w = W.config0()
     gpu = to_gpu(cpu_caches(w))
     out = {}
-    for scorer in ("tensor", "fma"):
+    for scorer in ("tensor", "tcgen05", "fma"):
         monkeypatch.setenv("KVC_B200_SCORER", scorer)
         m = bind(w, gpu, tmp_path)
         m.select_many(W.b200_requests(w))
         out[scorer] = [t.detach().clone().cpu() for t in m.last_stats]
-    for a, b in zip(out["tensor"][1:], out["fma"][1:]):  # mean, var, agg
-        finite = torch.isfinite(b)
-        assert_scores_close(a[finite], b[finite], tol=2e-4)
+    for tc in ("tensor", "tcgen05"):
+        for a, b in zip(out[tc][1:], out["fma"][1:]):  # mean, var, agg
+            finite = torch.isfinite(b)
+            assert_scores_close(a[finite], b[finite], tol=2e-4)
 
 
 def test_per_request_compress_equals_batched(tmp_path):
@@ -116,7 +120,7 @@ def test_per_request_compress_equals_batched(tmp_path):
         assert int(m2.staged_offsets[row]) == w.lengths[i] - w.options.kv_budget
 
 
-@pytest.mark.parametrize("scorer", ["tensor", "fma"])
+@pytest.mark.parametrize("scorer", ["tensor", "tcgen05", "fma"])
 def test_single_call_step_equals_entry_points_one_by_one(scorer, tmp_path, monkeypatch):
     """kvc_triattention_run launches exactly what the individual entry points do."""
     from vllm_ascend_kvcompress import _native as N
@@ -146,9 +150,10 @@ def test_single_call_step_equals_entry_points_one_by_one(scorer, tmp_path, monke
     if m2.use_tensor_scorer:
         frag = torch.empty(R * L * m2.local_kv_heads * m2.frag_block, dtype=torch.int32, device="cuda")
         K.prepare_score_fragments(m2.scoring_omega, m2.offsets, plan, m2.scoring_q_real, m2.scoring_q_imag,
-                                  m2.scoring_scale, m2.scoring_extra, m2.scoring_q_pass, m2.kv_dtype, frag)
+                                  m2.scoring_scale, m2.scoring_extra, m2.scoring_q_pass, m2.kv_dtype, frag,
+                                  tcgen05=m2.use_tcgen05)
         K.score_paged_keys_tc(m2._key_maps, L, m2.kv_dtype, m2.num_blocks, m2.local_kv_heads, m2.group,
-                              m2.head_dim, m2.rotary_dim, plan, frag, raw, partial, m2._err)
+                              m2.head_dim, m2.rotary_dim, plan, frag, raw, partial, m2._err, tcgen05=m2.use_tcgen05)
     else:
         coef = f32(R * L * m2.local_kv_heads * m2.coef_block)
         K.prepare_score_coefficients(m2.scoring_omega, m2.offsets, plan, m2.scoring_q_real, m2.scoring_q_imag,
@@ -378,8 +383,10 @@ def test_edge_cases_match_oracle(case, tmp_path):
     assert_compaction(w, cpu, gpu, {i: keep[row] for row, i in enumerate(idx)})
 
 
-def test_fp16_cache_and_padded_block_stride(tmp_path):
+@pytest.mark.parametrize("scorer", ["auto", "tcgen05"])
+def test_fp16_cache_and_padded_block_stride(scorer, tmp_path, monkeypatch):
     """K and V interleaved in one raw buffer with padding between pages, fp16."""
+    monkeypatch.setenv("KVC_B200_SCORER", scorer)
     w = _edge("padded_fp16", W.Geometry(2, 2, 10, 128, 128, 1e6),
               W.Options(kv_budget=512, protected_prefix_window=4, protected_recent_window=64, score_layer_stride=1),
               [900, 1700], 27)
@@ -413,8 +420,10 @@ def test_fp16_cache_and_padded_block_stride(tmp_path):
         assert bool((pad == -7.0).all()), "padding between pages must stay untouched"
 
 
-def test_fp16_partial_rope_matches_oracle(tmp_path):
+@pytest.mark.parametrize("scorer", ["auto", "tcgen05"])
+def test_fp16_partial_rope_matches_oracle(scorer, tmp_path, monkeypatch):
     """FP16 caches with partial RoPE (head_dim 256, rotary 64, 8 query heads per KV head)."""
+    monkeypatch.setenv("KVC_B200_SCORER", scorer)
     w = _edge("fp16_partial", W.Geometry(2, 1, 8, 256, 64, 1e7, model_type="qwen3_5_moe_text"),
               W.Options(kv_budget=768, protected_prefix_window=128, protected_recent_window=128,
                         score_layer_stride=1), [2100, 1500], 31, per=16)

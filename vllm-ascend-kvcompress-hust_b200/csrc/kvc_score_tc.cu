@@ -27,90 +27,25 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
-#include "kvc_async.cuh"
+#include "kvc_score_tc.cuh"
 
 namespace kvc {
 
 constexpr int kTcConsumers = 4;
 constexpr int kTcThreads = (kTcConsumers + 1) * 32;
-constexpr int kMaxTcLayers = 64;
-constexpr int kBoxElems = 64;                   // 128-byte swizzle span of 16-bit elements
-constexpr int kBoxBytes = kBoxElems * 2 * kBlock;  // one box: 128 tokens x 64 elements = 16 KB
-
-__host__ __device__ constexpr int frag_steps(int F, int P) { return 4 * (F / 16) + P / 16; }
+static_assert(kTcConsumers == kTcQuarters, "one moments partial per consumer warp");
 
 // ---------------------------------------------------------------------------
 // B-operand fragments of W (prepared once per (request, layer, head))
 // ---------------------------------------------------------------------------
 
-struct FragArgs {
-  const float* omega;     // [L][F]
-  const float* offsets;   // [n_off]
-  const int64_t* round_start;
-  const float* q_real;    // [L][kvh][G][F]
-  const float* q_imag;
-  const float* scale;
-  const float* extra;
-  const float* q_pass;    // [L][kvh][G][P] or null
-  uint32_t* frag;         // [R][L][kvh][S][32 lanes][4 words]
-  int n_off, R, L, kvh, G, F, P, half_fp16;
-};
-
-__device__ __forceinline__ uint16_t to_half_bits(float v, int fp16) {
-  if (fp16) {
-    __half h = __float2half_rn(v);
-    return *reinterpret_cast<uint16_t*>(&h);
-  }
-  __nv_bfloat16 b = __float2bfloat16_rn(v);
-  return *reinterpret_cast<uint16_t*>(&b);
-}
-
-__device__ __forceinline__ float from_half_bits(uint16_t v, int fp16) {
-  return fp16 ? unpack1(v, Fp16{}) : unpack1(v, Bf16{});
-}
-
 __global__ void __launch_bounds__(256) prepare_frag_kernel(const __grid_constant__ FragArgs a) {
   pdl_wait();  // the preceding kernel of the step has finished (see kvc_common.cuh)
   pdl_trigger();
   extern __shared__ float sm[];
-  float* cm = sm;                      // [F] mean cos
-  float* sn = sm + a.F;                // [F] mean sin
-  float* tc = sm + 2 * a.F;            // [n_off][F] cos
-  float* ts = tc + a.n_off * a.F;      // [n_off][F] sin
-  float* qs = ts + a.n_off * a.F;      // [4][G][F] q_real, q_imag, scale, extra of this (layer, head)
   const int l = blockIdx.x, r = blockIdx.y, h = blockIdx.z;
-  const float rs = (float)a.round_start[r];
-  {
-    const int gf = a.G * a.F;
-    const int64_t base = (int64_t)(l * a.kvh + h) * gf;
-    for (int i = threadIdx.x; i < gf; i += blockDim.x) {
-      qs[i] = a.q_real[base + i];
-      qs[gf + i] = a.q_imag[base + i];
-      qs[2 * gf + i] = a.scale[base + i];
-      qs[3 * gf + i] = a.extra[base + i];
-    }
-  }
-  for (int i = threadIdx.x; i < a.n_off * a.F; i += blockDim.x) {
-    const int o = i / a.F, f = i % a.F;
-    // fp32 (offset + round_start) then * omega, as the reference forms phases
-    const float ph = __fmul_rn(__fadd_rn(a.offsets[o], rs), a.omega[l * a.F + f]);
-    sincosf(ph, &ts[i], &tc[i]);
-  }
-  __syncthreads();
-  for (int f = threadIdx.x; f < a.F; f += blockDim.x) {
-    float cs = 0.f, ss = 0.f;
-    for (int o = 0; o < a.n_off; ++o) {  // offsets summed in order
-      cs += tc[o * a.F + f];
-      ss += ts[o * a.F + f];
-    }
-    const float inv = 1.0f / (float)a.n_off;
-    cm[f] = cs * inv;
-    sn[f] = ss * inv;
-  }
-  __syncthreads();
+  stage_w_inputs(a, sm, l, r, h);
   const int S = frag_steps(a.F, a.P);
-  const int kf = a.F / 16;
-  const int gf = a.G * a.F;
   for (int i = threadIdx.x; i < S * 32; i += blockDim.x) {
     const int lane = i % 32;
     const int s = i / 32;
@@ -120,24 +55,9 @@ __global__ void __launch_bounds__(256) prepare_frag_kernel(const __grid_constant
       for (int q = 0; q < 2; ++q) {        // register: k rows 0..7 / 8..15 of the step
         uint32_t word = 0;
         for (int e = 0; e < 2; ++e) {
-          const int k = 2 * (lane % 4) + 8 * q + e;  // row within the 16-row step
-          float v = 0.f;
+          const int k = 16 * s + 2 * (lane % 4) + 8 * q + e;  // K index of W
           bool lo_zero = false;
-          if (g < a.G) {
-            const int part = s < kf ? 0 : s < 2 * kf ? 1 : s < 3 * kf ? 2 : s < 4 * kf ? 3 : 4;
-            if (part < 4) {
-              const int f = (s - part * kf) * 16 + k;
-              const int src = g * a.F + f;
-              const float qr = qs[src], qi = qs[gf + src], sc = qs[2 * gf + src];
-              if (part == 0) v = sc * (qr * cm[f] - qi * sn[f]);
-              else if (part == 1) v = sc * (qi * cm[f] + qr * sn[f]);
-              else v = qs[3 * gf + src] * sc;
-              lo_zero = part == 3;  // m_lo rows pair with e_hi only
-            } else {
-              const int p = (s - 4 * kf) * 16 + k;
-              v = a.q_pass[((int64_t)(l * a.kvh + h) * a.G + g) * a.P + p];
-            }
-          }
+          const float v = g < a.G ? w_value(a, sm, l, h, g, k, lo_zero) : 0.f;
           const uint16_t hi = to_half_bits(v, a.half_fp16);
           uint16_t bits;
           if (t == 0) bits = hi;
@@ -156,14 +76,6 @@ __global__ void __launch_bounds__(256) prepare_frag_kernel(const __grid_constant
 // ---------------------------------------------------------------------------
 // PTX helpers (mbarrier, TMA, ldmatrix, mma)
 // ---------------------------------------------------------------------------
-
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* map, int c0, int c1, int c2, int c3,
-                                            uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
-      ::"r"(dst), "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
-      : "memory");
-}
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -190,63 +102,9 @@ __device__ __forceinline__ void mma16816<Fp16>(float (&d)[4], const uint32_t (&a
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ float sqrt_approx(float x) {
-  float y;
-  asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-__device__ __forceinline__ uint32_t pack2(float lo, float hi, Bf16) {
-  uint32_t d;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
-  return d;
-}
-__device__ __forceinline__ uint32_t pack2(float lo, float hi, Fp16) {
-  uint32_t d;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
-  return d;
-}
-
-// m = |(kr, ki)| for the 8 elements of an A fragment, split into hi + lo halves
-// (packed fp32x2 arithmetic: two elements per instruction).
-template <class E>
-__device__ __forceinline__ void modulus_split(const uint32_t (&kr)[4], const uint32_t (&ki)[4], uint32_t (&hi)[4],
-                                              uint32_t (&lo)[4]) {
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 r = unpack2(kr[i], E{});
-    const float2 m = unpack2(ki[i], E{});
-    float2 sq = __fmul2_rn(r, r);
-    sq = __ffma2_rn(m, m, sq);
-    const float2 mod = make_float2(sqrt_approx(sq.x), sqrt_approx(sq.y));
-    hi[i] = pack2(mod.x, mod.y, E{});
-    const float2 h = unpack2(hi[i], E{});
-    const float2 d = __ffma2_rn(h, make_float2(-1.f, -1.f), mod);
-    lo[i] = pack2(d.x, d.y, E{});
-  }
-}
-
 // ---------------------------------------------------------------------------
 // the scorer
 // ---------------------------------------------------------------------------
-
-struct TcArgs {
-  CUtensorMap maps[kMaxTcLayers];
-  const int64_t* src_blocks;
-  const int64_t* src_block_off;
-  const int32_t* tokens;
-  const int32_t* page_off;
-  const uint4* frag;
-  float* raw;
-  float* partial;
-  int32_t* error_flag;
-  int64_t tok_total;
-  int64_t num_blocks;
-  int64_t units;        // layers_here * kvh * total_pages
-  int layer0;           // global index of maps[0]
-  int L_total;          // scoring layers (raw / partial / frag indexing)
-  int kvh, G, R, total_pages;
-};
 
 template <int F, int P>
 struct TcGeom {
@@ -547,8 +405,14 @@ extern "C" int kvc_tc_supported(int group, int head_dim, int rotary_dim) {
   return tc_geometry_supported(group, head_dim, rotary_dim) ? 1 : 0;
 }
 
-// One moments partial per consumer warp's 32-token slice of a page.
-extern "C" int kvc_tc_partials_per_page(void) { return kTcConsumers; }
+extern "C" int kvc_tc05_supported(int group, int head_dim, int rotary_dim) {
+  const bool ok = group >= 1 && group <= 8 && rotary_dim % 2 == 0 && head_dim >= rotary_dim &&
+                  umma_geometry(rotary_dim / 2, head_dim - rotary_dim);
+  return ok ? 1 : 0;
+}
+
+// One moments partial per 32-token slice of a page (both tensor-core scorers).
+extern "C" int kvc_tc_partials_per_page(void) { return kTcQuarters; }
 
 extern "C" int64_t kvc_fragment_words(int num_freq, int pass_dim) {
   if (num_freq <= 0 || num_freq % 16 || pass_dim < 0 || pass_dim % 16) return 0;
@@ -583,11 +447,12 @@ extern "C" int kvc_encode_key_maps(const void* const* k_layers, int L, int dtype
   return KVC_OK;
 }
 
-extern "C" int kvc_prepare_score_fragments(const float* omega, const float* offsets, int n_off,
-                                           const int64_t* round_start, int R, int L, int kvh, int G, int F, int P,
-                                           const float* q_real, const float* q_imag, const float* scale,
-                                           const float* extra, const float* q_pass, int dtype, uint32_t* frag_out,
-                                           void* stream) {
+// W for either tensor-core scorer: mma.sync register fragments, or (umma) the
+// swizzled shared-memory matrix the tcgen05 scorer's descriptors read.
+static int prepare_fragments(bool umma, const float* omega, const float* offsets, int n_off,
+                             const int64_t* round_start, int R, int L, int kvh, int G, int F, int P,
+                             const float* q_real, const float* q_imag, const float* scale, const float* extra,
+                             const float* q_pass, int dtype, uint32_t* frag_out, void* stream) {
   KVC_CHECK_ARG(omega && offsets && round_start && q_real && q_imag && scale && extra && frag_out, KVC_ENULL);
   KVC_CHECK_ARG(n_off > 0 && n_off <= 64 && R >= 0 && L > 0 && kvh > 0 && G > 0 && G <= 8, KVC_EINVAL);
   KVC_CHECK_ARG(F > 0 && F % 16 == 0 && P >= 0 && P % 16 == 0, KVC_EUNSUPPORTED);
@@ -597,22 +462,45 @@ extern "C" int kvc_prepare_score_fragments(const float* omega, const float* offs
   if (R == 0) return KVC_OK;
   FragArgs a{omega, offsets, round_start, q_real, q_imag, scale, extra, q_pass, frag_out,
              n_off, R, L, kvh, G, F, P, dtype == KVC_FP16 ? 1 : 0};
-  const size_t smem = ((size_t)(2 + 2 * n_off) * F + (size_t)4 * G * F) * sizeof(float);
+  const size_t smem = w_stage_floats(n_off, F, G) * sizeof(float);
   KVC_CHECK_ARG(smem <= 48 * 1024, KVC_EUNSUPPORTED);
+  if (umma) {
+    KVC_CHECK_ARG(umma_geometry(F, P), KVC_EUNSUPPORTED);
+    return prepare_w_umma(a, (cudaStream_t)stream);
+  }
   launch_dep(prepare_frag_kernel, dim3(L, R, kvh), dim3(256), smem, (cudaStream_t)stream, a);
   return launch_status();
 }
 
-extern "C" int kvc_score_paged_keys_tc(const void* key_maps, int L, int dtype, int64_t num_blocks, int kvh, int G,
-                                       int D, int rot, const int64_t* src_blocks, const int64_t* src_block_off,
-                                       const int32_t* tokens, const int32_t* page_off, int R, int total_pages,
-                                       const uint32_t* frag, float* raw_out, float* partial_out,
-                                       int32_t* error_flag, void* stream) {
+extern "C" int kvc_prepare_score_fragments(const float* omega, const float* offsets, int n_off,
+                                           const int64_t* round_start, int R, int L, int kvh, int G, int F, int P,
+                                           const float* q_real, const float* q_imag, const float* scale,
+                                           const float* extra, const float* q_pass, int dtype, uint32_t* frag_out,
+                                           void* stream) {
+  return prepare_fragments(false, omega, offsets, n_off, round_start, R, L, kvh, G, F, P, q_real, q_imag, scale,
+                           extra, q_pass, dtype, frag_out, stream);
+}
+
+extern "C" int kvc_prepare_score_fragments_tc05(const float* omega, const float* offsets, int n_off,
+                                                const int64_t* round_start, int R, int L, int kvh, int G, int F,
+                                                int P, const float* q_real, const float* q_imag, const float* scale,
+                                                const float* extra, const float* q_pass, int dtype,
+                                                uint32_t* frag_out, void* stream) {
+  return prepare_fragments(true, omega, offsets, n_off, round_start, R, L, kvh, G, F, P, q_real, q_imag, scale,
+                           extra, q_pass, dtype, frag_out, stream);
+}
+
+static int score_tc(bool umma, const void* key_maps, int L, int dtype, int64_t num_blocks, int kvh, int G, int D,
+                    int rot, const int64_t* src_blocks, const int64_t* src_block_off, const int32_t* tokens,
+                    const int32_t* page_off, int R, int total_pages, const uint32_t* frag, float* raw_out,
+                    float* partial_out, int32_t* error_flag, void* stream) {
   KVC_CHECK_ARG(key_maps && src_blocks && src_block_off && tokens && page_off && frag && raw_out && partial_out,
                 KVC_ENULL);
   KVC_CHECK_ARG(L > 0 && kvh > 0 && R >= 0 && total_pages >= 0 && num_blocks > 0, KVC_EINVAL);
   KVC_CHECK_ARG(dtype == KVC_BF16 || dtype == KVC_FP16, KVC_EINVAL);
-  KVC_CHECK_ARG(tc_geometry_supported(G, D, rot), KVC_EUNSUPPORTED);
+  KVC_CHECK_ARG(umma ? G >= 1 && G <= 8 && rot % 2 == 0 && umma_geometry(rot / 2, D - rot)
+                     : tc_geometry_supported(G, D, rot),
+                KVC_EUNSUPPORTED);
   KVC_CHECK_ARG(aligned(frag, 16) && aligned(partial_out, 8), KVC_EALIGN);
   if (R == 0 || total_pages == 0) return KVC_OK;
   const unsigned char* maps = reinterpret_cast<const unsigned char*>(key_maps);
@@ -639,8 +527,28 @@ extern "C" int kvc_score_paged_keys_tc(const void* key_maps, int L, int dtype, i
     a.R = R;
     a.total_pages = total_pages;
     const int F = rot / 2, P = D - rot;
-    const int rc = dtype == KVC_BF16 ? dispatch_tc<Bf16>(a, F, P, st) : dispatch_tc<Fp16>(a, F, P, st);
+    const int rc = umma                ? launch_umma(a, F, P, dtype == KVC_FP16, st)
+                   : dtype == KVC_BF16 ? dispatch_tc<Bf16>(a, F, P, st)
+                                       : dispatch_tc<Fp16>(a, F, P, st);
     if (rc != KVC_OK) return rc;
   }
   return KVC_OK;
+}
+
+extern "C" int kvc_score_paged_keys_tc(const void* key_maps, int L, int dtype, int64_t num_blocks, int kvh, int G,
+                                       int D, int rot, const int64_t* src_blocks, const int64_t* src_block_off,
+                                       const int32_t* tokens, const int32_t* page_off, int R, int total_pages,
+                                       const uint32_t* frag, float* raw_out, float* partial_out,
+                                       int32_t* error_flag, void* stream) {
+  return score_tc(false, key_maps, L, dtype, num_blocks, kvh, G, D, rot, src_blocks, src_block_off, tokens, page_off,
+                  R, total_pages, frag, raw_out, partial_out, error_flag, stream);
+}
+
+extern "C" int kvc_score_paged_keys_tc05(const void* key_maps, int L, int dtype, int64_t num_blocks, int kvh, int G,
+                                         int D, int rot, const int64_t* src_blocks, const int64_t* src_block_off,
+                                         const int32_t* tokens, const int32_t* page_off, int R, int total_pages,
+                                         const uint32_t* frag, float* raw_out, float* partial_out,
+                                         int32_t* error_flag, void* stream) {
+  return score_tc(true, key_maps, L, dtype, num_blocks, kvh, G, D, rot, src_blocks, src_block_off, tokens, page_off,
+                  R, total_pages, frag, raw_out, partial_out, error_flag, stream);
 }

@@ -64,16 +64,18 @@ int score_stage(const kvc_triattention_step& s, void* const* ev, void* stream, b
   const int heads = s.kv_heads * s.group;
   int rc;
   mark(ev, 0, st);
-  if (s.scorer == KVC_SCORER_TENSOR) {
-    rc = kvc_prepare_score_fragments(s.omega, s.offsets, s.n_off, s.round_start, s.num_requests, s.score_layers,
-                                     s.kv_heads, s.group, F, P, s.q_real, s.q_imag, s.scale, s.extra, s.q_pass,
-                                     s.kv_dtype, (uint32_t*)s.score_coef, stream);
+  const bool tensor = s.scorer == KVC_SCORER_TENSOR || s.scorer == KVC_SCORER_TCGEN05;
+  if (tensor) {
+    const bool tc05 = s.scorer == KVC_SCORER_TCGEN05;
+    rc = (tc05 ? kvc_prepare_score_fragments_tc05 : kvc_prepare_score_fragments)(
+        s.omega, s.offsets, s.n_off, s.round_start, s.num_requests, s.score_layers, s.kv_heads, s.group, F, P,
+        s.q_real, s.q_imag, s.scale, s.extra, s.q_pass, s.kv_dtype, (uint32_t*)s.score_coef, stream);
     if (rc != KVC_OK) return rc;
     mark(ev, 1, st);
-    rc = kvc_score_paged_keys_tc(s.key_maps, s.score_layers, s.kv_dtype, s.num_blocks, s.kv_heads, s.group,
-                                 s.head_dim, s.rotary_dim, s.src_blocks, s.src_block_off, s.tokens, s.page_off,
-                                 s.num_requests, s.total_pages, (const uint32_t*)s.score_coef, s.raw, s.partial,
-                                 s.error_flag, stream);
+    rc = (tc05 ? kvc_score_paged_keys_tc05 : kvc_score_paged_keys_tc)(
+        s.key_maps, s.score_layers, s.kv_dtype, s.num_blocks, s.kv_heads, s.group, s.head_dim, s.rotary_dim,
+        s.src_blocks, s.src_block_off, s.tokens, s.page_off, s.num_requests, s.total_pages,
+        (const uint32_t*)s.score_coef, s.raw, s.partial, s.error_flag, stream);
   } else if (s.scorer == KVC_SCORER_FMA) {
     rc = kvc_prepare_score_coefficients(s.omega, s.offsets, s.n_off, s.round_start, s.num_requests, s.score_layers,
                                         s.kv_heads, s.group, F, s.q_real, s.q_imag, s.scale, s.extra,
@@ -90,7 +92,7 @@ int score_stage(const kvc_triattention_step& s, void* const* ev, void* stream, b
   if (rc != KVC_OK) return rc;
   mark(ev, 2, st);
   rc = kvc_head_stats(s.partial, s.score_layers, s.num_requests, s.total_pages,
-                      s.scorer == KVC_SCORER_TENSOR ? kvc_tc_partials_per_page() : 1, heads, s.tokens, s.page_off,
+                      tensor ? kvc_tc_partials_per_page() : 1, heads, s.tokens, s.page_off,
                       s.mean, s.var, s.den, stream);
   if (rc != KVC_OK) return rc;
   mark(ev, 3, st);

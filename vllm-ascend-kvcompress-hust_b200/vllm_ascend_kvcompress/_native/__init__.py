@@ -47,6 +47,12 @@ _SIGNATURES = {
     "kvc_score_paged_keys_tc": (
         c_int, [_P, c_int, c_int, c_int64, c_int, c_int, c_int, c_int, _P, _P, _P, _P, c_int, c_int, _P, _P, _P,
                 _P, _P]),
+    "kvc_tc05_supported": (c_int, [c_int, c_int, c_int]),
+    "kvc_prepare_score_fragments_tc05": (
+        c_int, [_P, _P, c_int, _P, c_int, c_int, c_int, c_int, c_int, c_int, _P, _P, _P, _P, _P, c_int, _P, _P]),
+    "kvc_score_paged_keys_tc05": (
+        c_int, [_P, c_int, c_int, c_int64, c_int, c_int, c_int, c_int, _P, _P, _P, _P, c_int, c_int, _P, _P, _P,
+                _P, _P]),
     "kvc_normalize_aggregate": (c_int, [_P, c_int, c_int, c_int, _P, _P, _P, _P, c_int, c_int, _P, _P, _P]),
     "kvc_aggregate_rows": (c_int, [_P, c_int, c_int, _P, _P, c_int, c_int, _P, _P]),
     "kvc_select_keep": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int, _P, _P, _P]),
@@ -84,7 +90,7 @@ _SIGNATURES = {
     "kvc_triattention_run": (c_int, [_P, c_int, _P, _P]),
 }
 
-SCORER_TENSOR, SCORER_FMA = 0, 1
+SCORER_TENSOR, SCORER_FMA, SCORER_TCGEN05 = 0, 1, 2
 STAGE_SCORE, STAGE_AGGREGATE, STAGE_SELECT, STAGE_COMPACT, STAGE_TABLES, STAGE_ALL = 1, 2, 4, 8, 16, 31
 STAGE_EXCHANGE = 32
 STEP_EVENTS = 8

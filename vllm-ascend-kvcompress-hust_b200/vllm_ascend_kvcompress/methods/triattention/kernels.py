@@ -208,6 +208,11 @@ def tc_supported(group: int, head_dim: int, rotary_dim: int) -> bool:
     return bool(N.lib().kvc_tc_supported(group, head_dim, rotary_dim))
 
 
+def tc05_supported(group: int, head_dim: int, rotary_dim: int) -> bool:
+    """Geometries of the tcgen05 (TMEM-accumulator) scorer."""
+    return bool(N.lib().kvc_tc05_supported(group, head_dim, rotary_dim))
+
+
 def encode_key_maps(k_ptrs, dtype: torch.dtype, block_stride: int, num_blocks: int, kvh: int, head_dim: int):
     """Host buffer of one 128-byte TMA descriptor per K cache (built once per binding)."""
     import ctypes
@@ -223,23 +228,25 @@ def fragment_words(num_freq: int, pass_dim: int) -> int:
 
 
 def prepare_score_fragments(omega, offsets, plan: BatchPlan, q_real, q_imag, scale, extra, q_pass,
-                            dtype: torch.dtype, frag_out) -> None:
+                            dtype: torch.dtype, frag_out, tcgen05: bool = False) -> None:
+    """W of the tensor-core scorer (tcgen05=True: the layout kvc_score_paged_keys_tc05 reads)."""
     L, kvh, G, F = q_real.shape
     P = 0 if q_pass is None else q_pass.shape[-1]
-    N.check(N.lib().kvc_prepare_score_fragments(
+    name = "kvc_prepare_score_fragments_tc05" if tcgen05 else "kvc_prepare_score_fragments"
+    N.check(getattr(N.lib(), name)(
         _p(omega), _p(offsets), offsets.numel(), _p(plan.round_start), plan.num_requests, L, kvh, G, F, P,
         _p(q_real), _p(q_imag), _p(scale), _p(extra), _p(q_pass), _dtype_code(dtype), _p(frag_out), _stream()),
-        "kvc_prepare_score_fragments")
+        name)
 
 
 def score_paged_keys_tc(key_maps, num_layers: int, dtype: torch.dtype, num_blocks: int, kvh: int, group: int,
                         head_dim: int, rotary_dim: int, plan: BatchPlan, frag, raw_out, partial_out,
-                        error_flag) -> None:
-    N.check(N.lib().kvc_score_paged_keys_tc(
+                        error_flag, tcgen05: bool = False) -> None:
+    name = "kvc_score_paged_keys_tc05" if tcgen05 else "kvc_score_paged_keys_tc"
+    N.check(getattr(N.lib(), name)(
         key_maps, num_layers, _dtype_code(dtype), num_blocks, kvh, group, head_dim, rotary_dim,
         _p(plan.src_blocks), _p(plan.src_off), _p(plan.tokens), _p(plan.page_off), plan.num_requests,
-        plan.total_pages, _p(frag), _p(raw_out), _p(partial_out), _p(error_flag), _stream()),
-        "kvc_score_paged_keys_tc")
+        plan.total_pages, _p(frag), _p(raw_out), _p(partial_out), _p(error_flag), _stream()), name)
 
 
 def head_stats(partial, num_layers: int, heads: int, plan: BatchPlan, mean_out, var_out, den_out,

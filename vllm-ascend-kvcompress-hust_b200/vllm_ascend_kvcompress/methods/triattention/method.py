@@ -536,14 +536,18 @@ class TriAttentionMethod(KVCompressionMethod):
         self.layer_aggregation_code = N.AGG_MEAN if self.config.layer_aggregation == "mean" else N.AGG_MAX
         self.coef_block = K.coef_floats(self.num_freq, self.group, self.offsets.numel(), self.score_aggregation_code)
         choice = os.environ.get(_SCORER_ENV, self.scorer)
-        if choice not in ("auto", "tensor", "fma"):
-            raise ValueError(f"{_SCORER_ENV} must be auto, tensor or fma")
+        if choice not in ("auto", "tensor", "tcgen05", "fma"):
+            raise ValueError(f"{_SCORER_ENV} must be auto, tensor, tcgen05 or fma")
+        supported = K.tc05_supported if choice == "tcgen05" else K.tc_supported
         tc_ok = (self.config.score_aggregation == "mean"
-                 and K.tc_supported(self.group, self.head_dim, self.rotary_dim)
+                 and supported(self.group, self.head_dim, self.rotary_dim)
                  and (self.block_stride * 2) % 16 == 0)
-        if choice == "tensor" and not tc_ok:
-            raise RuntimeError("the tensor-core scorer does not support this geometry/aggregation")
+        if choice in ("tensor", "tcgen05") and not tc_ok:
+            raise RuntimeError(f"the {choice} scorer does not support this geometry/aggregation")
         self.use_tensor_scorer = tc_ok and choice != "fma"
+        # "auto"/"tensor": the mma.sync kernel (measured faster on this contraction);
+        # "tcgen05": the TMEM-accumulator kernel
+        self.use_tcgen05 = self.use_tensor_scorer and choice == "tcgen05"
         if self.use_tensor_scorer:
             self._key_maps = K.encode_key_maps(self._k_score, self.kv_dtype, self.block_stride, self.num_blocks,
                                                self.local_kv_heads, self.head_dim)
@@ -616,7 +620,8 @@ class TriAttentionMethod(KVCompressionMethod):
         """Fill the bound-once fields of the native step descriptor."""
         cfg = self.config
         st = N.TriAttentionStep()
-        st.scorer = N.SCORER_TENSOR if self.use_tensor_scorer else N.SCORER_FMA
+        st.scorer = (N.SCORER_TCGEN05 if self.use_tcgen05 else
+                     N.SCORER_TENSOR if self.use_tensor_scorer else N.SCORER_FMA)
         st.kv_dtype = K._dtype_code(self.kv_dtype)
         st.score_layers = self.scoring_layer_count
         st.kv_heads = self.local_kv_heads
