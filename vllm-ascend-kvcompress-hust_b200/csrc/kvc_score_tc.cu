@@ -257,41 +257,46 @@ __global__ void __launch_bounds__(kTcThreads, TcGeom<F, P>::kMinBlocks) score_tc
     const uint32_t stage = stage0 + s * Gm::kStageBytes;
     const uint4* wl = wsm + lane;
 
-    float y[2][4];
+    // accumulators per 16-token tile mt: kr/ki products in the hi / lo column
+    // halves (c0, c1), modulus products likewise (c2, c3); the pass band adds
+    // to c0 / c1.  W fragments are loaded once per K step for both tiles.
+    float c0[2][4] = {}, c1[2][4] = {}, c2[2][4] = {}, c3[2][4] = {};
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt) {
-      const int row0 = warp * 32 + mt * 16;
-      // independent accumulator chains: kr, ki, modulus (and pass), hi/lo column halves
-      float ar0[4] = {}, ar1[4] = {}, ai0[4] = {}, ai1[4] = {}, am0[4] = {}, am1[4] = {};
+    for (int j = 0; j < KF; ++j) {
+      const uint4 wa = wl[j * 32], wb = wl[(KF + j) * 32];
+      const uint4 we = wl[(2 * KF + j) * 32], wf = wl[(3 * KF + j) * 32];
 #pragma unroll
-      for (int j = 0; j < KF; ++j) {
+      for (int mt = 0; mt < 2; ++mt) {
+        const int row0 = warp * 32 + mt * 16;
         uint32_t kr[4], ki[4], mh[4], ml[4];
         ldsm_x4(frag_addr(stage, row0, 16 * j, lane), kr);
         ldsm_x4(frag_addr(stage, row0, F + 16 * j, lane), ki);
-        const uint4 wa = wl[j * 32], wb = wl[(KF + j) * 32];
-        mma16816<E>(ar0, kr, wa.x, wa.y);
-        mma16816<E>(ar1, kr, wa.z, wa.w);
-        mma16816<E>(ai0, ki, wb.x, wb.y);
-        mma16816<E>(ai1, ki, wb.z, wb.w);
+        mma16816<E>(c0[mt], kr, wa.x, wa.y);
+        mma16816<E>(c1[mt], kr, wa.z, wa.w);
+        mma16816<E>(c0[mt], ki, wb.x, wb.y);
+        mma16816<E>(c1[mt], ki, wb.z, wb.w);
         modulus_split<E>(kr, ki, mh, ml);
-        const uint4 we = wl[(2 * KF + j) * 32], wf = wl[(3 * KF + j) * 32];
-        mma16816<E>(am0, mh, we.x, we.y);
-        mma16816<E>(am1, mh, we.z, we.w);
-        mma16816<E>(am0, ml, wf.x, wf.y);
+        mma16816<E>(c2[mt], mh, we.x, we.y);
+        mma16816<E>(c3[mt], mh, we.z, we.w);
+        mma16816<E>(c2[mt], ml, wf.x, wf.y);
       }
-      float ap0[4] = {}, ap1[4] = {};
-#pragma unroll
-      for (int j = 0; j < KP; ++j) {
-        uint32_t kp[4];
-        ldsm_x4(frag_addr(stage, row0, 2 * F + 16 * j, lane), kp);
-        const uint4 wp = wl[(4 * KF + j) * 32];
-        mma16816<E>(ap0, kp, wp.x, wp.y);
-        mma16816<E>(ap1, kp, wp.z, wp.w);
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        y[mt][i] = ((ar0[i] + ar1[i]) + (ai0[i] + ai1[i])) + ((am0[i] + am1[i]) + (ap0[i] + ap1[i]));
     }
+#pragma unroll
+    for (int j = 0; j < KP; ++j) {
+      const uint4 wp = wl[(4 * KF + j) * 32];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        uint32_t kp[4];
+        ldsm_x4(frag_addr(stage, warp * 32 + mt * 16, 2 * F + 16 * j, lane), kp);
+        mma16816<E>(c0[mt], kp, wp.x, wp.y);
+        mma16816<E>(c1[mt], kp, wp.z, wp.w);
+      }
+    }
+    float y[2][4];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) y[mt][i] = (c0[mt][i] + c1[mt][i]) + (c2[mt][i] + c3[mt][i]);
     __syncwarp();
     if (lane == 0) mbar_arrive(empty0 + 8 * s);
 
