@@ -186,8 +186,9 @@ int kvc_head_stats(const float* partial, int num_layers, int num_requests, int t
  * heads, one row per scoring layer: rows_out [L][total_pages*128] (required;
  * also the tensor-parallel all-reduce input).  When agg_out is non-NULL the
  * layers are then reduced (sequential sum then / L, or max) and finalised
- * (NaN -> -inf, +inf -> 1e30) into agg_out [total_pages*128]
- * (kvc_aggregate_rows on the same stream).
+ * (NaN -> -inf, +inf -> 1e30) into agg_out [total_pages*128], 16-byte
+ * aligned (kvc_aggregate_rows on the same stream; with one layer the
+ * normalisation kernel writes agg_out itself).
  * Replaces aggregate_normalized_scores (methods/triattention/kernels.py:407-437),
  * TriAttentionMethod._aggregate_torch (methods/triattention/method.py:477-503)
  * and the finalisation at methods/triattention/method.py:463-467.

@@ -29,19 +29,22 @@ __device__ __forceinline__ float div_by(float a, float b, float rcp) {
   return __fmaf_rn(r, rcp, q0);
 }
 
-struct NormPages {
-  int req[kNormPages];
-  int64_t start[kNormPages];  // first token of the page's request in the padded space
-  int ntok[kNormPages];
+template <int NP>
+struct NormPagesN {
+  int req[NP];
+  int64_t start[NP];  // first token of the page's request in the padded space
+  int ntok[NP];
 };
+using NormPages = NormPagesN<kNormPages>;
 
-// Stage the CTA's page table and layer l's statistics ([kNormPages][heads] mean,
-// den, 1/den in `st`).  Every thread of the CTA calls it; it ends synchronised.
-__device__ __forceinline__ void norm_stage(NormPages& np, float* st, int page0, int l, int heads, int total_pages,
-                                           int R, const int32_t* __restrict__ tokens,
-                                           const int32_t* __restrict__ page_off, const float* __restrict__ mean,
-                                           const float* __restrict__ den) {
-  if (threadIdx.x < kNormPages) {
+// Stage the CTA's page table and layer l's statistics ([NP][heads] mean, den,
+// 1/den in `st`).  Every thread of the CTA calls it; it ends synchronised.
+template <int NP>
+__device__ __forceinline__ void norm_stage_n(NormPagesN<NP>& np, float* st, int page0, int l, int heads,
+                                             int total_pages, int R, const int32_t* __restrict__ tokens,
+                                             const int32_t* __restrict__ page_off, const float* __restrict__ mean,
+                                             const float* __restrict__ den) {
+  if (threadIdx.x < NP) {
     const int p = page0 + threadIdx.x;
     int r = 0;
     if (p < total_pages) {
@@ -53,9 +56,9 @@ __device__ __forceinline__ void norm_stage(NormPages& np, float* st, int page0, 
   }
   __syncthreads();
   float* mu_s = st;
-  float* dn_s = st + kNormPages * heads;
-  float* rc_s = st + 2 * kNormPages * heads;
-  for (int i = threadIdx.x; i < kNormPages * heads; i += blockDim.x) {
+  float* dn_s = st + NP * heads;
+  float* rc_s = st + 2 * NP * heads;
+  for (int i = threadIdx.x; i < NP * heads; i += blockDim.x) {
     const int slot = i / heads;
     if (page0 + slot >= total_pages) continue;
     const int64_t g = ((int64_t)l * R + np.req[slot]) * heads + i % heads;
@@ -65,6 +68,13 @@ __device__ __forceinline__ void norm_stage(NormPages& np, float* st, int page0, 
     rc_s[i] = __frcp_rn(d);
   }
   __syncthreads();
+}
+
+__device__ __forceinline__ void norm_stage(NormPages& np, float* st, int page0, int l, int heads, int total_pages,
+                                           int R, const int32_t* __restrict__ tokens,
+                                           const int32_t* __restrict__ page_off, const float* __restrict__ mean,
+                                           const float* __restrict__ den) {
+  norm_stage_n<kNormPages>(np, st, page0, l, heads, total_pages, R, tokens, page_off, mean, den);
 }
 
 // This thread's 4 tokens of layer l: their token index `tok` in the padded
@@ -106,6 +116,60 @@ __device__ __forceinline__ int norm_quad(const NormPages& np, const float* st, c
   }
   z = make_float4(t + 0 < n ? m4.x : 0.f, t + 1 < n ? m4.y : 0.f, t + 2 < n ? m4.z : 0.f, t + 3 < n ? m4.w : 0.f);
   return min(4, n - t);
+}
+
+// norm_quad with the heads shared by HS adjacent lanes: the thread of
+// (quad, slice) covers heads slice, slice + HS, ..., and the HS lanes of a
+// quad combine their maxima by shuffles (every lane of the warp must call it).
+// Pages of NP per CTA, 32 quads of 4 tokens per page.  Returns the valid
+// token count of the quad; z is complete in every lane of the quad.
+template <int NP, int HS>
+__device__ __forceinline__ int norm_quad_split(const NormPagesN<NP>& np, const float* st,
+                                               const float* __restrict__ raw, int l, int heads, int total_pages,
+                                               int page0, int quad, int slice, int64_t& tok, float4& z) {
+  const int slot = quad >> 5;
+  const int p = page0 + slot;
+  tok = (int64_t)p * kBlock + (quad & 31) * 4;
+  float4 m4 = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+  int t = 0, n = 0;
+  if (p < total_pages) {
+    t = (int)(tok - np.start[slot]);
+    n = np.ntok[slot];
+    const float* mu = st + slot * heads;
+    const float* dn = st + NP * heads + slot * heads;
+    const float* rc = st + 2 * NP * heads + slot * heads;
+    const float4* rl = reinterpret_cast<const float4*>(raw + ((int64_t)l * total_pages + p) * heads * kBlock +
+                                                       (tok & (kBlock - 1)));
+    if (t < n) {
+      constexpr int U = HS == 1 ? 4 : 2;  // heads of this slice whose loads are in flight together
+      for (int h0 = slice; h0 < heads; h0 += U * HS) {
+        float4 x[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k)
+          if (h0 + k * HS < heads) x[k] = __ldg(rl + (int64_t)(h0 + k * HS) * (kBlock / 4));
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+          const int h = h0 + k * HS;
+          if (h < heads) {
+            const float m = mu[h], d = dn[h], c = rc[h];
+            m4.x = nan_max(m4.x, div_by(x[k].x - m, d, c));
+            m4.y = nan_max(m4.y, div_by(x[k].y - m, d, c));
+            m4.z = nan_max(m4.z, div_by(x[k].z - m, d, c));
+            m4.w = nan_max(m4.w, div_by(x[k].w - m, d, c));
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 1; o < HS; o <<= 1) {
+    m4.x = nan_max(m4.x, __shfl_xor_sync(0xffffffffu, m4.x, o));
+    m4.y = nan_max(m4.y, __shfl_xor_sync(0xffffffffu, m4.y, o));
+    m4.z = nan_max(m4.z, __shfl_xor_sync(0xffffffffu, m4.z, o));
+    m4.w = nan_max(m4.w, __shfl_xor_sync(0xffffffffu, m4.w, o));
+  }
+  z = make_float4(t + 0 < n ? m4.x : 0.f, t + 1 < n ? m4.y : 0.f, t + 2 < n ? m4.z : 0.f, t + 3 < n ? m4.w : 0.f);
+  return t < n ? min(4, n - t) : 0;
 }
 
 }  // namespace kvc

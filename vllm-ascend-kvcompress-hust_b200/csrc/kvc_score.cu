@@ -405,7 +405,6 @@ __global__ void __launch_bounds__(1024) head_stats_kernel(const float* __restric
   pdl_wait();  // the preceding kernel of the step has finished (see kvc_common.cuh)
   pdl_trigger();
   extern __shared__ double red[];  // [blockDim]
-  __shared__ double mean_s[1024];
   const int l = blockIdx.x, r = blockIdx.y;
   const int p0 = page_off[r], p1 = page_off[r + 1], T = tokens[r];
   const int span = kBlock / parts;  // tokens per partial
@@ -417,26 +416,10 @@ __global__ void __launch_bounds__(1024) head_stats_kernel(const float* __restric
   const int q0 = p0 * parts;
   const int q1 = min(p1 * parts, q0 + (T + span - 1) / span);  // padding partials hold nothing
   constexpr int U = 8;  // partials whose loads are in flight together
-  // pass 1: sum of partial sums
-  double s = 0.0;
-  if (live) {
-    for (int q = q0 + j; q < q1; q += U * slots) {
-      float x[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int qq = q + u * slots;
-        x[u] = qq < q1 ? __ldg(part + (int64_t)qq * heads + h).x : 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) s += (double)x[u];
-    }
-  }
-  s = reduce_slots(live ? s : 0.0, red, heads, slots);
-  if (threadIdx.x < heads) mean_s[threadIdx.x] = T > 0 ? s / T : 0.0;
-  __syncthreads();
-  const double mu = mean_s[h];
-  // pass 2: sum of squares about the overall mean
-  double m2 = 0.0;
+  // one pass in fp64: S = sum of the partial sums, Q = sum over partials of
+  // (M2_b + s_b^2 / n_b); then M2 = Q - S^2 / T (Chan's combination of all
+  // partials about the overall mean, expanded)
+  double s = 0.0, q2 = 0.0;
   if (live) {
     for (int q = q0 + j; q < q1; q += U * slots) {
       float2 v[U];
@@ -450,17 +433,22 @@ __global__ void __launch_bounds__(1024) head_stats_kernel(const float* __restric
         const int qq = q + u * slots;
         if (qq < q1) {
           const int n = min(span, T - (qq - q0) * span);
-          const double d = (double)v[u].x / n - mu;
-          m2 += (double)v[u].y + n * d * d;
+          const double x = (double)v[u].x;
+          s += x;
+          q2 += (double)v[u].y + x * x / n;
         }
       }
     }
   }
-  m2 = reduce_slots(live ? m2 : 0.0, red, heads, slots);
+  s = reduce_slots(live ? s : 0.0, red, heads, slots);
+  q2 = reduce_slots(live ? q2 : 0.0, red, heads, slots);
+  // valid in the first `heads` threads (reduce_slots returns there)
+  const double mu = T > 0 ? s / T : 0.0;
+  const double m2 = fmax(0.0, q2 - s * mu);
   if (threadIdx.x < heads) {
     const int64_t i = ((int64_t)l * R + r) * heads + threadIdx.x;
     const float var = T > 0 ? (float)(m2 / T) : NAN;
-    mean_out[i] = T > 0 ? (float)mean_s[threadIdx.x] : NAN;
+    mean_out[i] = T > 0 ? (float)mu : NAN;
     var_out[i] = var;
     den_out[i] = sqrtf(fmaxf(var, 1e-6f));
   }
@@ -475,24 +463,36 @@ __global__ void __launch_bounds__(1024) head_stats_kernel(const float* __restric
 // writes the layer's row; aggregate_rows then reduces the layers (TP = 1 and
 // the NCCL sync).  Page padding is written as 0, keeping rows finite for the
 // MAX sync.
+// HS lanes share a token quad's heads (HS = 1: one lane takes all heads of 4
+// tokens); a 256-thread CTA covers 256 / (32 * HS) pages.  Small batches use
+// HS = 4 for four times the CTAs; large ones HS = 1 (less staging per page).
+// agg: with a single scoring layer the layer aggregation is the identity, so
+// the final score finalize(z) is written here too (null: rows only).
+template <int HS>
 __global__ void __launch_bounds__(256) normalize_kernel(const float* __restrict__ raw, int L, int heads,
                                                         int total_pages, const float* __restrict__ mean,
                                                         const float* __restrict__ den,
                                                         const int32_t* __restrict__ tokens,
                                                         const int32_t* __restrict__ page_off, int R,
-                                                        float* rows) {
+                                                        float* rows, float* agg) {
   pdl_wait();  // the preceding kernel of the step has finished (see kvc_common.cuh)
   pdl_trigger();
-  extern __shared__ float st[];  // [3][kNormPages][heads]
-  __shared__ NormPages np;
+  constexpr int NP = 256 / (32 * HS);
+  extern __shared__ float st[];  // [3][NP][heads]
+  __shared__ NormPagesN<NP> np;
   const int l = blockIdx.y;
-  const int page0 = blockIdx.x * kNormPages;
-  norm_stage(np, st, page0, l, heads, total_pages, R, tokens, page_off, mean, den);
-  if (page0 + (int)(threadIdx.x >> 5) >= total_pages) return;
+  const int page0 = blockIdx.x * NP;
+  norm_stage_n<NP>(np, st, page0, l, heads, total_pages, R, tokens, page_off, mean, den);
+  const int quad = threadIdx.x / HS, slice = threadIdx.x % HS;
+  if (page0 + (quad >> 5) >= total_pages) return;  // warp-uniform: a warp's quads share a page
   int64_t tok;
   float4 z;
-  norm_quad(np, st, raw, l, heads, total_pages, page0, tok, z);
+  norm_quad_split<NP, HS>(np, st, raw, l, heads, total_pages, page0, quad, slice, tok, z);
+  if (slice != 0) return;
   *reinterpret_cast<float4*>(rows + (int64_t)l * total_pages * kBlock + tok) = z;
+  if (agg)  // padding is 0 in z and stays 0
+    *reinterpret_cast<float4*>(agg + tok) =
+        make_float4(finalize_score(z.x), finalize_score(z.y), finalize_score(z.z), finalize_score(z.w));
 }
 
 __global__ void __launch_bounds__(256) aggregate_rows_kernel(const float* __restrict__ rows, int L,
@@ -682,14 +682,24 @@ extern "C" int kvc_normalize_aggregate(const float* raw, int L, int heads, int t
   KVC_CHECK_ARG(layer_aggregation == KVC_AGG_MEAN || layer_aggregation == KVC_AGG_MAX, KVC_EINVAL);
   if (R == 0 || total_pages == 0) return KVC_OK;
   KVC_CHECK_ARG(aligned(raw, 16) && aligned(rows_out, 16), KVC_EALIGN);
-  const dim3 grid((unsigned)((total_pages + kNormPages - 1) / kNormPages), (unsigned)L);
-  const size_t smem = (size_t)3 * kNormPages * heads * sizeof(float);
+  KVC_CHECK_ARG(agg_out == nullptr || aligned(agg_out, 16), KVC_EALIGN);
+  // fewer than two CTAs per SM with 8 pages each: split the heads instead
+  const bool split = (int64_t)((total_pages + 7) / 8) * L < 2 * (int64_t)sm_count();
+  const int np = split ? 2 : 8;
+  const dim3 grid((unsigned)((total_pages + np - 1) / np), (unsigned)L);
+  const size_t smem = (size_t)3 * np * heads * sizeof(float);
   if (smem > 48 * 1024) return KVC_EUNSUPPORTED;
   cudaStream_t st = (cudaStream_t)stream;
-  launch_dep(normalize_kernel, grid, dim3(256), smem, st, raw, L, heads, total_pages, mean, denom, tokens, page_off, R,
-             rows_out);
+  const bool fused = agg_out != nullptr && L == 1;  // one layer: no separate layer reduction
+  float* agg = fused ? agg_out : nullptr;
+  if (split)
+    launch_dep(normalize_kernel<4>, grid, dim3(256), smem, st, raw, L, heads, total_pages, mean, denom, tokens,
+               page_off, R, rows_out, agg);
+  else
+    launch_dep(normalize_kernel<1>, grid, dim3(256), smem, st, raw, L, heads, total_pages, mean, denom, tokens,
+               page_off, R, rows_out, agg);
   const int rc = launch_status();
-  if (rc != KVC_OK || agg_out == nullptr) return rc;
+  if (rc != KVC_OK || agg_out == nullptr || fused) return rc;
   return kvc_aggregate_rows(rows_out, L, total_pages, tokens, page_off, R, layer_aggregation, agg_out, stream);
 }
 

@@ -57,7 +57,9 @@ inline void mark(void* const* events, int slot, cudaStream_t st) {
 
 // push: the peer exchange follows, so normalisation delivers each quad's head
 // max to the inbox of the rank that owns it instead of writing local rows.
-int score_stage(const kvc_triattention_step& s, void* const* ev, void* stream, bool push) {
+// agg: with one scoring layer, normalisation also writes the aggregate (the
+// layer reduction is the identity), so the aggregate stage launches nothing.
+int score_stage(const kvc_triattention_step& s, void* const* ev, void* stream, bool push, float* agg) {
   cudaStream_t st = (cudaStream_t)stream;
   const int F = s.rotary_dim / 2;
   const int P = s.head_dim - s.rotary_dim;
@@ -102,7 +104,7 @@ int score_stage(const kvc_triattention_step& s, void* const* ev, void* stream, b
                             s.num_requests, s.peer_inbox, s.peer_flags, s.world, s.rank, s.epoch, stream);
   }
   return kvc_normalize_aggregate(s.raw, s.score_layers, heads, s.total_pages, s.mean, s.den, s.tokens, s.page_off,
-                                 s.num_requests, s.layer_aggregation, s.rows, nullptr, stream);
+                                 s.num_requests, s.layer_aggregation, s.rows, agg, stream);
 }
 
 }  // namespace
@@ -131,15 +133,18 @@ extern "C" int kvc_triattention_run(const kvc_triattention_step* step, int stage
     rc = tables_stage(s, st);
     if (rc != KVC_OK) return rc;
   }
+  const bool fuse_agg = (stages & KVC_STAGE_SCORE) && (stages & KVC_STAGE_AGGREGATE) && s.score_layers == 1;
   if (stages & KVC_STAGE_SCORE) {
-    rc = score_stage(s, ev, stream, (stages & KVC_STAGE_EXCHANGE) != 0);
+    rc = score_stage(s, ev, stream, (stages & KVC_STAGE_EXCHANGE) != 0, fuse_agg ? s.agg : nullptr);
     if (rc != KVC_OK) return rc;
   }
   if (stages & KVC_STAGE_AGGREGATE) {
     mark(ev, 4, st);
-    rc = kvc_aggregate_rows(s.rows, s.score_layers, s.total_pages, s.tokens, s.page_off, s.num_requests,
-                            s.layer_aggregation, s.agg, stream);
-    if (rc != KVC_OK) return rc;
+    if (!fuse_agg) {
+      rc = kvc_aggregate_rows(s.rows, s.score_layers, s.total_pages, s.tokens, s.page_off, s.num_requests,
+                              s.layer_aggregation, s.agg, stream);
+      if (rc != KVC_OK) return rc;
+    }
   }
   if (stages & KVC_STAGE_EXCHANGE) {
     mark(ev, 4, st);
