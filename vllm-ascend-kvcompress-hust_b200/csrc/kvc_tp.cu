@@ -135,19 +135,24 @@ __global__ void __launch_bounds__(256) tp_push_rows_kernel(const __grid_constant
   __shared__ float* inbox_s[KVC_TP_MAX_WORLD];
   for (int p = threadIdx.x; p < a.world; p += blockDim.x) inbox_s[p] = a.inbox[p];
   const int l = blockIdx.y;
-  const int page0 = blockIdx.x * kNormPages;
-  norm_stage(np, st, page0, l, a.heads, a.total_pages, a.R, a.tokens, a.page_off, a.mean, a.den);
-  int64_t tok;
-  float4 z;
-  if (norm_quad(np, st, a.raw, l, a.heads, a.total_pages, page0, tok, z) > 0) {
-    const int64_t q = tok >> 2;
-    const int o = (int)(q / a.per);
-    float* dst = inbox_s[o] + (((int64_t)a.rank * a.L + l) * a.per + (q - (int64_t)o * a.per)) * 4;
-    *reinterpret_cast<float4*>(dst) = z;  // a peer store unless this rank owns the quad
+  // grid-stride over 8-page groups: few CTAs, so one system fence per CTA
+  for (int page0 = blockIdx.x * kNormPages; page0 < a.total_pages; page0 += gridDim.x * kNormPages) {
+    norm_stage(np, st, page0, l, a.heads, a.total_pages, a.R, a.tokens, a.page_off, a.mean, a.den);
+    int64_t tok;
+    float4 z;
+    if (norm_quad(np, st, a.raw, l, a.heads, a.total_pages, page0, tok, z) > 0) {
+      const int64_t q = tok >> 2;
+      const int o = (int)(q / a.per);
+      float* dst = inbox_s[o] + (((int64_t)a.rank * a.L + l) * a.per + (q - (int64_t)o * a.per)) * 4;
+      *reinterpret_cast<float4*>(dst) = z;  // a peer store unless this rank owns the quad
+    }
+    __syncthreads();  // np / st are restaged for the next group
   }
-  __threadfence_system();  // this thread's stores before the completion count
+  // the CTA barrier orders every thread's stores before thread 0's system fence,
+  // which is cumulative over them (release pattern), then the completion count
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     int32_t* counter = a.flags[a.rank] + tp_push_counter(a.world);
     if (atomicAdd(counter, 1) == (int)(gridDim.x * gridDim.y) - 1) {
       atomicExch(counter, 0);
@@ -248,9 +253,11 @@ __global__ void __launch_bounds__(kTpThreads) tp_reduce_push_kernel(const __grid
       __syncthreads();  // part / done are rewritten by the next group
     }
   }
-  __threadfence_system();  // this thread's peer stores before the completion count
+  // the CTA barrier orders every thread's peer stores before thread 0's
+  // system fence, which is cumulative over them, then the completion count
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     int32_t* counter = mine + tp_exch_counter(world);
     if (atomicAdd(counter, 1) == (int)gridDim.x - 1) {
       atomicExch(counter, 0);
@@ -339,8 +346,11 @@ extern "C" int kvc_tp_push_rows(const float* raw, int num_layers, int heads, int
   a.world = world;
   a.rank = rank;
   a.epoch = epoch;
-  // every rank launches every step, even with no tokens, so the epochs of all ranks advance together
-  const dim3 grid((unsigned)std::max(1, (total_pages + kNormPages - 1) / kNormPages), (unsigned)num_layers);
+  // every rank launches every step, even with no tokens, so the epochs of all ranks advance together;
+  // about four CTAs per SM over all layers, each striding over 8-page groups
+  const int groups = std::max(1, (total_pages + kNormPages - 1) / kNormPages);
+  const int per_layer = std::max(1, std::min(groups, (4 * sm_count() + num_layers - 1) / num_layers));
+  const dim3 grid((unsigned)per_layer, (unsigned)num_layers);
   launch_dep(tp_push_rows_kernel, grid, dim3(256), smem, (cudaStream_t)stream, a);
   return launch_status();
 }
