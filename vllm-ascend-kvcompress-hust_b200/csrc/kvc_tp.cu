@@ -347,9 +347,11 @@ extern "C" int kvc_tp_push_rows(const float* raw, int num_layers, int heads, int
   a.rank = rank;
   a.epoch = epoch;
   // every rank launches every step, even with no tokens, so the epochs of all ranks advance together;
-  // about four CTAs per SM over all layers, each striding over 8-page groups
+  // up to eight CTAs per SM (the thread limit) over all layers, each striding
+  // over 8-page groups: each group is a chain of dependent loads (request
+  // lookup, head statistics, raw scores), so many CTAs in flight hide it
   const int groups = std::max(1, (total_pages + kNormPages - 1) / kNormPages);
-  const int per_layer = std::max(1, std::min(groups, (4 * sm_count() + num_layers - 1) / num_layers));
+  const int per_layer = std::max(1, std::min(groups, (8 * sm_count() + num_layers - 1) / num_layers));
   const dim3 grid((unsigned)per_layer, (unsigned)num_layers);
   launch_dep(tp_push_rows_kernel, grid, dim3(256), smem, (cudaStream_t)stream, a);
   return launch_status();
