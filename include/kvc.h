@@ -118,7 +118,12 @@ int kvc_score_paged_keys(const void* const* k_layers, int num_layers, int dtype,
  * {(64,0), (32,0), (32,192), (32,64), (64,128), (128,0)}).
  *   key_maps     host array of num_layers 128-byte TMA descriptors from
  *                kvc_encode_key_maps (built once per cache binding).
- *   frag         kvc_prepare_score_fragments output.
+ *   frag         kvc_prepare_score_fragments output: per (request, layer, KV
+ *                head) kvc_fragment_words(num_freq, pass_dim) words of 16-bit
+ *                coefficients; with an fp16 cache they are scaled by a power of
+ *                two (largest magnitude in [2^13, 2^14)) so low-|q| heads keep
+ *                their hi/lo split out of fp16's subnormals, and the scorer
+ *                undoes the scale exactly.
  *   partial_out  [L][total_pages*parts][kvh*G][2]: (sum, sum of squared
  *                deviations from the partial's mean) per 128/parts-token slice
  *                of each page, parts = kvc_tc_partials_per_page() (the

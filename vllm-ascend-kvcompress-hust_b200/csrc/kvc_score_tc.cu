@@ -44,8 +44,13 @@ __global__ void __launch_bounds__(256) prepare_frag_kernel(const __grid_constant
   pdl_trigger();
   extern __shared__ float sm[];
   const int l = blockIdx.x, r = blockIdx.y, h = blockIdx.z;
+  __shared__ float red[8];
   stage_w_inputs(a, sm, l, r, h);
+  const float scale = w_scale(a, sm, l, h, red);
   const int S = frag_steps(a.F, a.P);
+  // this (request, layer, head)'s record: S*32 uint4 of fragments, then the inverse scale
+  uint4* rec = reinterpret_cast<uint4*>(a.frag) + ((int64_t)(r * a.L + l) * a.kvh + h) * (S * 32 + 1);
+  if (threadIdx.x == 0) rec[S * 32] = make_uint4(__float_as_uint(1.f / scale), 0u, 0u, 0u);
   for (int i = threadIdx.x; i < S * 32; i += blockDim.x) {
     const int lane = i % 32;
     const int s = i / 32;
@@ -57,7 +62,7 @@ __global__ void __launch_bounds__(256) prepare_frag_kernel(const __grid_constant
         for (int e = 0; e < 2; ++e) {
           const int k = 16 * s + 2 * (lane % 4) + 8 * q + e;  // K index of W
           bool lo_zero = false;
-          const float v = g < a.G ? w_value(a, sm, l, h, g, k, lo_zero) : 0.f;
+          const float v = g < a.G ? w_value(a, sm, l, h, g, k, lo_zero) * scale : 0.f;
           const uint16_t hi = to_half_bits(v, a.half_fp16);
           uint16_t bits;
           if (t == 0) bits = hi;
@@ -67,9 +72,7 @@ __global__ void __launch_bounds__(256) prepare_frag_kernel(const __grid_constant
         words[2 * t + q] = word;
       }
     }
-    uint4* dst = reinterpret_cast<uint4*>(a.frag) +
-                 (((int64_t)(r * a.L + l) * a.kvh + h) * S + s) * 32 + lane;
-    *dst = make_uint4(words[0], words[1], words[2], words[3]);
+    rec[s * 32 + lane] = make_uint4(words[0], words[1], words[2], words[3]);
   }
 }
 
@@ -132,7 +135,9 @@ __device__ __forceinline__ uint32_t frag_addr(uint32_t stage, int row0, int dim0
 // Unit metadata the producer hands to the consumers with each stage.
 struct UnitMeta {
   int p, h, lg, valid, wgen, end;
+  float scale;  // undoes the W scaling of the unit's (request, layer, head)
 };
+static_assert(sizeof(UnitMeta) <= 32, "32 bytes of metadata per stage");
 
 // Pipeline (per CTA): one producer lane resolves its contiguous range of
 // (layer, head, page) units, publishes each unit's metadata and issues the
@@ -179,6 +184,7 @@ __global__ void __launch_bounds__(kTcThreads, TcGeom<F, P>::kMinBlocks) score_tc
     const int64_t u1 = min64(a.units, u0 + per);
     uint32_t it = 0;
     int r = 0, cur_key = -1, gen = -1;
+    float wscale = 1.f;
     bool ok = true;
     for (int64_t u = u0; u < u1 && ok; ++u) {
       const int p = (int)(u % a.total_pages);
@@ -198,13 +204,14 @@ __global__ void __launch_bounds__(kTcThreads, TcGeom<F, P>::kMinBlocks) score_tc
       if (new_w) {
         cur_key = key;
         ++gen;
+        wscale = __ldg(reinterpret_cast<const float*>(a.frag + (int64_t)key * (Gm::S * 32 + 1) + Gm::S * 32));
       }
       const int s = it % Gm::kStages;
       if (!mbar_wait(empty0 + 8 * s, ((it / Gm::kStages) & 1) ^ 1, a.error_flag)) {
         ok = false;
         break;
       }
-      meta[s] = UnitMeta{p, h, lg, min(kBlock, __ldg(a.tokens + r) - pl * kBlock), gen, 0};
+      meta[s] = UnitMeta{p, h, lg, min(kBlock, __ldg(a.tokens + r) - pl * kBlock), gen, 0, wscale};
       mbar_expect_tx(full0 + 8 * s, Gm::kStageBytes);
 #pragma unroll
       for (int b = 0; b < Gm::kBoxes; ++b)
@@ -218,7 +225,7 @@ __global__ void __launch_bounds__(kTcThreads, TcGeom<F, P>::kMinBlocks) score_tc
           break;
         }
         mbar_expect_tx(wfull, Gm::kWBytes);
-        bulk_load(wbuf, a.frag + (int64_t)key * Gm::S * 32, Gm::kWBytes, wfull);
+        bulk_load(wbuf, a.frag + (int64_t)key * (Gm::S * 32 + 1), Gm::kWBytes, wfull);
       }
     }
     if (ok) {  // sentinel stage: tells the consumers the range is done
@@ -312,7 +319,7 @@ __global__ void __launch_bounds__(kTcThreads, TcGeom<F, P>::kMinBlocks) score_tc
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int t = warp * 32 + (i >> 1) * 16 + (i & 1) * 8 + (lane >> 2);
-        vals[i] = y[i >> 1][(i & 1) * 2 + gi];
+        vals[i] = y[i >> 1][(i & 1) * 2 + gi] * mu.scale;  // exact: a power of two
         ok[i] = t < mu.valid && g < a.G;
       }
       float sum = 0.f;
@@ -421,7 +428,7 @@ extern "C" int kvc_tc_partials_per_page(void) { return kTcQuarters; }
 
 extern "C" int64_t kvc_fragment_words(int num_freq, int pass_dim) {
   if (num_freq <= 0 || num_freq % 16 || pass_dim < 0 || pass_dim % 16) return 0;
-  return (int64_t)frag_steps(num_freq, pass_dim) * 32 * 4;
+  return w_record_bytes(num_freq, pass_dim) / 4;
 }
 
 extern "C" int kvc_encode_key_maps(const void* const* k_layers, int L, int dtype, int64_t block_stride,

@@ -22,6 +22,11 @@ constexpr int kTcQuarters = 4;                     // moments partials per page 
 // 16-deep K steps of W: a, b, e, e_hi bands of F each, then the pass band
 __host__ __device__ constexpr int frag_steps(int F, int P) { return 4 * (F / 16) + P / 16; }
 
+// One (request, layer, head) record of W: frag_steps * 512 bytes of 16-bit
+// values, then 16 bytes whose first float is the exact power of two that
+// undoes W's scaling (w_scale); the scorers multiply their sums by it.
+__host__ __device__ constexpr int64_t w_record_bytes(int F, int P) { return (int64_t)frag_steps(F, P) * 512 + 16; }
+
 struct FragArgs {
   const float* omega;     // [L][F]
   const float* offsets;   // [n_off]
@@ -31,7 +36,7 @@ struct FragArgs {
   const float* scale;
   const float* extra;
   const float* q_pass;    // [L][kvh][G][P] or null
-  uint32_t* frag;         // per (request, layer, head): frag_steps * 512 bytes
+  uint32_t* frag;         // per (request, layer, head): a record of w_record_bytes
   int n_off, R, L, kvh, G, F, P, half_fp16;
 };
 
@@ -130,6 +135,32 @@ __device__ __forceinline__ float w_value(const FragArgs& a, const float* sm, int
   }
   const int p = k - 4 * a.F;
   return a.q_pass[((int64_t)(l * a.kvh + h) * a.G + g) * a.P + p];
+}
+
+// Power of two applied to W of (layer l, head h) before its 16-bit hi/lo
+// split.  fp16 has a narrow exponent range: coefficients of low-|q| heads
+// (1e-4 .. 1e-6) would fall into its subnormals and lose the lo half, so W
+// is scaled until its largest magnitude lies in [2^13, 2^14).  bf16 keeps
+// fp32's range and takes scale 1.  All threads call it (it synchronises).
+__device__ __forceinline__ float w_scale(const FragArgs& a, const float* sm, int l, int h, float* red) {
+  if (!a.half_fp16) return 1.f;
+  const int kw = 4 * a.F + a.P;
+  float m = 0.f;
+  for (int i = threadIdx.x; i < a.G * kw; i += blockDim.x) {
+    bool lo_zero;
+    m = fmaxf(m, fabsf(w_value(a, sm, l, h, i / kw, i % kw, lo_zero)));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  m = 0.f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
+  __syncthreads();
+  if (!(m > 0.f) || !isfinite(m)) return 1.f;
+  int e;
+  frexpf(m, &e);  // m = f * 2^e, f in [0.5, 1)
+  return ldexpf(1.f, max(-100, min(100, 14 - e)));
 }
 
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* map, int c0, int c1, int c2, int c3,

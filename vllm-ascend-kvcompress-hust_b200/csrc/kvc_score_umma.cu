@@ -49,6 +49,7 @@ constexpr int kSmemBudget = 220 * 1024;
 
 struct UMeta {
   int p, h, lg, valid, wgen, skip;
+  float scale;  // undoes the W scaling of the unit's (request, layer, head)
 };
 
 template <int F, int P>
@@ -170,9 +171,14 @@ __global__ void __launch_bounds__(256) prepare_w_umma_kernel(const __grid_consta
   pdl_trigger();
   extern __shared__ float sm[];
   const int l = blockIdx.x, r = blockIdx.y, h = blockIdx.z;
+  __shared__ float red[8];
   stage_w_inputs(a, sm, l, r, h);
+  const float scale = w_scale(a, sm, l, h, red);
   const int KW = 4 * a.F + a.P;
-  uint8_t* dst = reinterpret_cast<uint8_t*>(a.frag) + ((int64_t)(r * a.L + l) * a.kvh + h) * KW * 32;
+  // this (request, layer, head)'s record: the swizzled matrix, then the inverse scale
+  uint8_t* dst = reinterpret_cast<uint8_t*>(a.frag) + ((int64_t)(r * a.L + l) * a.kvh + h) * w_record_bytes(a.F, a.P);
+  if (threadIdx.x == 0)
+    *reinterpret_cast<uint4*>(dst + (int64_t)KW * 32) = make_uint4(__float_as_uint(1.f / scale), 0u, 0u, 0u);
   for (int i = threadIdx.x; i < 16 * (KW / 8); i += blockDim.x) {
     const int n = i & 15;      // row: n < 8 hi half of head n, else lo half of head n - 8
     const int k0 = (i >> 4) * 8;
@@ -180,7 +186,7 @@ __global__ void __launch_bounds__(256) prepare_w_umma_kernel(const __grid_consta
     uint32_t words[4] = {0u, 0u, 0u, 0u};
     for (int e = 0; e < 8; ++e) {
       bool lo_zero = false;
-      const float v = g < a.G ? w_value(a, sm, l, h, g, k0 + e, lo_zero) : 0.f;
+      const float v = g < a.G ? w_value(a, sm, l, h, g, k0 + e, lo_zero) * scale : 0.f;
       const uint16_t hi = to_half_bits(v, a.half_fp16);
       const uint16_t bits =
           n < 8 ? hi : lo_zero ? (uint16_t)0 : to_half_bits(v - from_half_bits(hi, a.half_fp16), a.half_fp16);
@@ -253,6 +259,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) score_umma_kernel(const __gri
     if (lane == 0) {
       uint32_t it = 0;  // units published
       int r = 0, cur_key = -1, gen = -1, loaded = -1;
+      float wscale = 1.f;
       for (int64_t u = u0; u < u0 + n; ++u) {
         const int p = (int)(u % a.total_pages);
         const int h = (int)((u / a.total_pages) % a.kvh);
@@ -267,7 +274,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) score_umma_kernel(const __gri
         if (blk < 0 || blk >= a.num_blocks) {
           // the unit still takes its turn (no copy, no MMA), so every role counts the same units
           raise_flag(a.error_flag, KVC_DEV_BLOCK_RANGE);
-          meta[s] = UMeta{p, h, lg, 0, gen, 1};
+          meta[s] = UMeta{p, h, lg, 0, gen, 1, 1.f};
           mbar_arrive(full0 + 8 * s);
           ++it;
           continue;
@@ -277,8 +284,10 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) score_umma_kernel(const __gri
         if (new_w) {
           cur_key = key;
           ++gen;
+          wscale = __ldg(reinterpret_cast<const float*>(a.frag + (int64_t)key * (Gm::kWBytes / 16 + 1) +
+                                                        Gm::kWBytes / 16));
         }
-        meta[s] = UMeta{p, h, lg, min(kBlock, __ldg(a.tokens + r) - pl * kBlock), gen, 0};
+        meta[s] = UMeta{p, h, lg, min(kBlock, __ldg(a.tokens + r) - pl * kBlock), gen, 0, wscale};
         mbar_expect_tx(full0 + 8 * s, Gm::kStageBytes);
 #pragma unroll
         for (int b = 0; b < Gm::kBoxes; ++b)
@@ -291,7 +300,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) score_umma_kernel(const __gri
           const int wb = gen & 1;
           if (gen >= 2 && !mbar_wait(wfree0 + 8 * wb, ((gen >> 1) - 1) & 1, a.error_flag)) break;
           mbar_expect_tx(wfull0 + 8 * wb, Gm::kWBytes);
-          bulk_load(wbuf0 + wb * Gm::kWBytes, a.frag + (int64_t)key * (Gm::kWBytes / 16), Gm::kWBytes,
+          bulk_load(wbuf0 + wb * Gm::kWBytes, a.frag + (int64_t)key * (Gm::kWBytes / 16 + 1), Gm::kWBytes,
                     wfull0 + 8 * wb);
           loaded = gen;
         }
@@ -471,7 +480,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) score_umma_kernel(const __gri
           uint32_t v[16];
           tmem_ld16(acol + 2 * F, v);
 #pragma unroll
-          for (int g = 0; g < 8; ++g) y[g] = __uint_as_float(v[g]) + __uint_as_float(v[8 + g]);
+          for (int g = 0; g < 8; ++g) y[g] = (__uint_as_float(v[g]) + __uint_as_float(v[8 + g])) * cur.scale;
         }
         if (more) form_a(nxt);  // the MMAs of unit k have read A; its accumulator is in y
         if (!cur.skip) epilogue(cur, y);
