@@ -127,24 +127,34 @@ struct PushArgs {
   int32_t epoch;
 };
 
+// QPT quads per thread per page group (8 * QPT pages): with few local heads
+// the per-group staging (request lookup, head statistics) and the per-quad
+// store dominate, so each thread takes several quads to amortise them and
+// keep more loads in flight.  The arithmetic per quad is norm_quad's.
+template <int QPT>
 __global__ void __launch_bounds__(256) tp_push_rows_kernel(const __grid_constant__ PushArgs a) {
   pdl_wait();  // the preceding kernel of the step has finished (see kvc_common.cuh)
   pdl_trigger();
-  extern __shared__ float st[];  // [3][kNormPages][heads]
-  __shared__ NormPages np;
+  constexpr int NP = 8 * QPT;
+  extern __shared__ float st[];  // [3][NP][heads]
+  __shared__ NormPagesN<NP> np;
   __shared__ float* inbox_s[KVC_TP_MAX_WORLD];
   for (int p = threadIdx.x; p < a.world; p += blockDim.x) inbox_s[p] = a.inbox[p];
   const int l = blockIdx.y;
-  // grid-stride over 8-page groups: few CTAs, so one system fence per CTA
-  for (int page0 = blockIdx.x * kNormPages; page0 < a.total_pages; page0 += gridDim.x * kNormPages) {
-    norm_stage(np, st, page0, l, a.heads, a.total_pages, a.R, a.tokens, a.page_off, a.mean, a.den);
-    int64_t tok;
-    float4 z;
-    if (norm_quad(np, st, a.raw, l, a.heads, a.total_pages, page0, tok, z) > 0) {
-      const int64_t q = tok >> 2;
-      const int o = (int)(q / a.per);
-      float* dst = inbox_s[o] + (((int64_t)a.rank * a.L + l) * a.per + (q - (int64_t)o * a.per)) * 4;
-      *reinterpret_cast<float4*>(dst) = z;  // a peer store unless this rank owns the quad
+  // grid-stride over page groups: few CTAs, so one system fence per CTA
+  for (int page0 = blockIdx.x * NP; page0 < a.total_pages; page0 += gridDim.x * NP) {
+    norm_stage_n<NP>(np, st, page0, l, a.heads, a.total_pages, a.R, a.tokens, a.page_off, a.mean, a.den);
+#pragma unroll
+    for (int i = 0; i < QPT; ++i) {
+      int64_t tok;
+      float4 z;
+      if (norm_quad_split<NP, 1>(np, st, a.raw, l, a.heads, a.total_pages, page0, threadIdx.x + 256 * i, 0, tok,
+                                 z) > 0) {
+        const int64_t q = tok >> 2;
+        const int o = (int)(q / a.per);
+        float* dst = inbox_s[o] + (((int64_t)a.rank * a.L + l) * a.per + (q - (int64_t)o * a.per)) * 4;
+        *reinterpret_cast<float4*>(dst) = z;  // a peer store unless this rank owns the quad
+      }
     }
     __syncthreads();  // np / st are restaged for the next group
   }
@@ -328,7 +338,9 @@ extern "C" int kvc_tp_push_rows(const float* raw, int num_layers, int heads, int
                     epoch > 0,
                 KVC_EINVAL);
   KVC_CHECK_ARG(aligned(raw, 16), KVC_EALIGN);
-  const size_t smem = (size_t)3 * kNormPages * heads * sizeof(float);
+  const int qpt = heads <= 8 ? 4 : heads <= 16 ? 2 : 1;  // quads per thread per page group
+  const int np = 8 * qpt;
+  const size_t smem = (size_t)3 * np * heads * sizeof(float);
   KVC_CHECK_ARG(smem <= 48 * 1024, KVC_EUNSUPPORTED);
   PushArgs a{};
   a.raw = raw;
@@ -348,12 +360,15 @@ extern "C" int kvc_tp_push_rows(const float* raw, int num_layers, int heads, int
   a.epoch = epoch;
   // every rank launches every step, even with no tokens, so the epochs of all ranks advance together;
   // up to eight CTAs per SM (the thread limit) over all layers, each striding
-  // over 8-page groups: each group is a chain of dependent loads (request
+  // over page groups: each group is a chain of dependent loads (request
   // lookup, head statistics, raw scores), so many CTAs in flight hide it
-  const int groups = std::max(1, (total_pages + kNormPages - 1) / kNormPages);
+  const int groups = std::max(1, (total_pages + np - 1) / np);
   const int per_layer = std::max(1, std::min(groups, (8 * sm_count() + num_layers - 1) / num_layers));
   const dim3 grid((unsigned)per_layer, (unsigned)num_layers);
-  launch_dep(tp_push_rows_kernel, grid, dim3(256), smem, (cudaStream_t)stream, a);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (qpt == 4) launch_dep(tp_push_rows_kernel<4>, grid, dim3(256), smem, st, a);
+  else if (qpt == 2) launch_dep(tp_push_rows_kernel<2>, grid, dim3(256), smem, st, a);
+  else launch_dep(tp_push_rows_kernel<1>, grid, dim3(256), smem, st, a);
   return launch_status();
 }
 
