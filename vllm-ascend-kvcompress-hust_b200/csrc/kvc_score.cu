@@ -387,12 +387,19 @@ __global__ void __launch_bounds__(kScoreWarps * 32) score_max_kernel(const __gri
 // (the exact decomposition of the sum of squares about the overall mean), then
 // var = M2 / T (population variance, as torch.var_mean(correction=0)).
 __device__ __forceinline__ double reduce_slots(double v, double* red, int heads, int slots) {
-  // sum of the `slots` per-thread values of each head, slot order fixed; returns it to slot 0 threads
+  // sum of the `slots` per-thread values of each head (thread j * heads + h
+  // holds slot j of head h) by a pairwise tree in a fixed order; returns it to
+  // the slot-0 threads (threadIdx.x < heads)
   red[threadIdx.x] = v;
   __syncthreads();
-  double s = 0.0;
-  if (threadIdx.x < heads)
-    for (int j = 0; j < slots; ++j) s += red[j * heads + threadIdx.x];
+  const int j = threadIdx.x / heads;
+  int half = 1;
+  while (half < slots) half <<= 1;
+  for (half >>= 1; half >= 1; half >>= 1) {
+    if (j < half && j + half < slots) red[threadIdx.x] += red[threadIdx.x + half * heads];
+    __syncthreads();
+  }
+  const double s = red[threadIdx.x];
   __syncthreads();
   return s;
 }
