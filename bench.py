@@ -867,8 +867,10 @@ def b200_arm(args) -> None:
         if tf.is_file() and args.config == 1 and args.seqs == 32 and args.layers == 48 and world == 1:
             traffic = json.loads(tf.read_text()).get("compact_kernel_bytes_per_launch_config1")
         # tables, prepare, score, head stats, normalise, the layer reduction (or
-        # the peer exchange kernel), select, compact
-        launches_per_step = 8
+        # the peer exchange kernel), select, compact; with one scoring layer at
+        # N = 1 normalisation writes the aggregate itself (no layer reduction)
+        scoring_layers = -(-w.geometry.num_layers // w.options.score_layer_stride)
+        launches_per_step = 7 if (world == 1 and scoring_layers == 1) else 8
         line = {
             "metric": METRIC, "value": s["value"], "unit": UNIT, "value_is": "aggregate over all GPUs",
             "per_gpu": s["per_gpu"], "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
