@@ -46,6 +46,23 @@ def test_coef_floats_layout():
     assert lib.kvc_coef_floats(64, 5, 17, 1) == 64 * 16 + 17 * 64 * 10
 
 
+def test_fragment_record_and_scorer_geometries():
+    """Per (request, layer, KV head): 16-bit coefficients of 4F + P rows x 16
+    columns, then one 16-byte record holding the inverse W scale."""
+    lib = N.lib()
+    assert lib.kvc_fragment_words(64, 0) == (4 * 64 * 16 * 2 + 16) // 4
+    assert lib.kvc_fragment_words(32, 192) == ((4 * 32 + 192) * 16 * 2 + 16) // 4
+    assert lib.kvc_fragment_words(30, 0) == 0  # F must be a multiple of 16
+    # the mma.sync scorer instantiates head_dim 256 full RoPE; the tcgen05 one
+    # (512 TMEM columns over three warpgroups) does not
+    assert lib.kvc_tc_supported(5, 128, 128) == 1 and lib.kvc_tc05_supported(5, 128, 128) == 1
+    assert lib.kvc_tc_supported(8, 256, 64) == 1 and lib.kvc_tc05_supported(8, 256, 64) == 1
+    assert lib.kvc_tc_supported(4, 256, 256) == 1 and lib.kvc_tc05_supported(4, 256, 256) == 0
+    assert lib.kvc_tc05_supported(9, 128, 128) == 0  # query group above 8
+    assert lib.kvc_tc05_supported(5, 128, 127) == 0  # odd rotary dim
+    assert lib.kvc_tc_partials_per_page() == 4
+
+
 def test_host_validation_rejects_without_launch():
     lib = N.lib()
     fake = ctypes.c_void_p(0x1000)
