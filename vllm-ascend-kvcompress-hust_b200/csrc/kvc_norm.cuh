@@ -2,18 +2,18 @@
 // (kvc_normalize_aggregate) and the tensor-parallel push (kvc_tp_push_rows), so
 // both produce bit-identical values.
 //
-// A CTA of 256 threads covers 8 pages of one scoring layer: one thread per 4
-// consecutive tokens, loading each query head's raw scores of its 4 tokens as
-// one 16-byte vector (page-major raw: a page's 128 scores of one head are
-// contiguous).  The request of each page and its per-head mean, denominator
-// and reciprocal for the layer are staged in shared memory first.
+// A CTA of 256 threads covers NP pages of one scoring layer; each token quad
+// (4 consecutive tokens) is handled by HS lanes that split its query heads, or
+// (HS = 1) one lane may take several quads.  A lane loads each of its heads'
+// raw scores of the 4 tokens as one 16-byte vector (page-major raw: a page's
+// 128 scores of one head are contiguous).  The request of each page and its
+// per-head mean, denominator and reciprocal for the layer are staged in shared
+// memory first (norm_stage_n).
 #pragma once
 
 #include "kvc_common.cuh"
 
 namespace kvc {
-
-constexpr int kNormPages = 8;  // pages per CTA (256 threads x 4 tokens)
 
 // a / b from the correctly rounded reciprocal rcp = RN(1/b): q0 = RN(a * rcp),
 // residual r = a - q0 * b (exact by FMA), q = RN(q0 + r * rcp).  Markstein's
@@ -35,7 +35,6 @@ struct NormPagesN {
   int64_t start[NP];  // first token of the page's request in the padded space
   int ntok[NP];
 };
-using NormPages = NormPagesN<kNormPages>;
 
 // Stage the CTA's page table and layer l's statistics ([NP][heads] mean, den,
 // 1/den in `st`).  Every thread of the CTA calls it; it ends synchronised.
@@ -70,57 +69,12 @@ __device__ __forceinline__ void norm_stage_n(NormPagesN<NP>& np, float* st, int 
   __syncthreads();
 }
 
-__device__ __forceinline__ void norm_stage(NormPages& np, float* st, int page0, int l, int heads, int total_pages,
-                                           int R, const int32_t* __restrict__ tokens,
-                                           const int32_t* __restrict__ page_off, const float* __restrict__ mean,
-                                           const float* __restrict__ den) {
-  norm_stage_n<kNormPages>(np, st, page0, l, heads, total_pages, R, tokens, page_off, mean, den);
-}
-
-// This thread's 4 tokens of layer l: their token index `tok` in the padded
-// space, and the head max of (raw - mean) / den for the valid ones (0 for page
-// padding).  Returns the number of valid tokens (0: padding or past the pages).
-__device__ __forceinline__ int norm_quad(const NormPages& np, const float* st, const float* __restrict__ raw, int l,
-                                         int heads, int total_pages, int page0, int64_t& tok, float4& z) {
-  const int slot = threadIdx.x >> 5;  // 32 threads x 4 tokens per page
-  const int p = page0 + slot;
-  z = make_float4(0.f, 0.f, 0.f, 0.f);
-  tok = (int64_t)p * kBlock + (threadIdx.x & 31) * 4;
-  if (p >= total_pages) return 0;
-  const int t = (int)(tok - np.start[slot]);
-  const int n = np.ntok[slot];
-  if (t >= n) return 0;
-  const float* mu = st + slot * heads;
-  const float* dn = st + kNormPages * heads + slot * heads;
-  const float* rc = st + 2 * kNormPages * heads + slot * heads;
-  const float4* rl = reinterpret_cast<const float4*>(raw + ((int64_t)l * total_pages + p) * heads * kBlock +
-                                                     (tok & (kBlock - 1)));
-  constexpr int U = 4;  // heads whose loads are in flight together (16 floats per thread)
-  float4 m4 = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-  for (int h0 = 0; h0 < heads; h0 += U) {
-    float4 x[U];
-#pragma unroll
-    for (int k = 0; k < U; ++k)
-      if (h0 + k < heads) x[k] = __ldg(rl + (int64_t)(h0 + k) * (kBlock / 4));
-#pragma unroll
-    for (int k = 0; k < U; ++k) {
-      const int h = h0 + k;
-      if (h < heads) {
-        const float m = mu[h], d = dn[h], c = rc[h];
-        m4.x = nan_max(m4.x, div_by(x[k].x - m, d, c));
-        m4.y = nan_max(m4.y, div_by(x[k].y - m, d, c));
-        m4.z = nan_max(m4.z, div_by(x[k].z - m, d, c));
-        m4.w = nan_max(m4.w, div_by(x[k].w - m, d, c));
-      }
-    }
-  }
-  z = make_float4(t + 0 < n ? m4.x : 0.f, t + 1 < n ? m4.y : 0.f, t + 2 < n ? m4.z : 0.f, t + 3 < n ? m4.w : 0.f);
-  return min(4, n - t);
-}
-
-// norm_quad with the heads shared by HS adjacent lanes: the thread of
+// The head max of (raw - mean) / den for the 4 tokens of quad `quad` of the
+// CTA's pages (its token index in the padded space in `tok`; 0 for page
+// padding), with the heads shared by HS adjacent lanes: the thread of
 // (quad, slice) covers heads slice, slice + HS, ..., and the HS lanes of a
-// quad combine their maxima by shuffles (every lane of the warp must call it).
+// quad combine their maxima by shuffles (every lane of the warp must call it
+// when HS > 1).
 // Pages of NP per CTA, 32 quads of 4 tokens per page.  Returns the valid
 // token count of the quad; z is complete in every lane of the quad.
 template <int NP, int HS>
